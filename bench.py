@@ -1,0 +1,452 @@
+"""Benchmark: propose_with_update rows/s on BASELINE config 2
+(B=256, S=8192, k=16, P=32, R=128, 8 backoff candidates, factor 2.0,
+min_token_prob 0.1) on 1..8 GPUs of one node.
+
+One bench step is one propose_with_update over the B=256 rows of a decode
+step. Steps run as CUDA-graph replays of the fused kernel; they rotate over
+32 independent replicas of the [256, 8192] token buffer (256 MiB, above the
+126 MB L2), each replica advancing through the config's 100-step decode
+loop, so every step reads its rows from HBM. With N GPUs every rank drafts
+its own 256 rows (weak scaling, no collective on the data path) and the
+reported value is all rows of all ranks / max-over-ranks time.
+
+``--impl reference`` times the reference algorithm's CPU path instead (the
+numpy restatement in oracle/, parallel over rows on the host cores) on a
+bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B, S, T, K = 256, 8192, 5, 16
+DECODE_STEPS = 100
+NREP = 32
+METRIC = "propose_with_update rows/s (B=256,S=8192)"
+CONFIG = {"workload": "config2: local-only propose_with_update, B=256, "
+                      "S=8192, k=16, P=32, R=128, C=8, factor=2.0, "
+                      "min_prob=0.1, 100-step decode loop",
+          "global_batch": B, "seq_len": S,
+          "l2": "inputs larger than L2: 32 rotating replicas x 8 MiB"}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=12800)
+    ap.add_argument("--warmup", type=int, default=320)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=400)
+    ap.add_argument("--cpu-rows", type=int, default=256,
+                    help="rows per step in the CPU sample")
+    ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--no-e2e", action="store_true",
+                    help="skip the end-to-end API leg (profiling runs)")
+    ap.add_argument("--no-cpu", action="store_true",
+                    help="skip the CPU baseline leg (profiling runs)")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+def workload(rank: int):
+    from suffixgpu_b200 import workloads as wl
+    return wl.config2(seed=2 + 1000 * rank, steps=DECODE_STEPS)
+
+
+def algorithmic_bytes(data, rep_shift) -> np.ndarray:
+    """Per-decode-step algorithmic bytes for every replica: the committed
+    row read once for drafting rows (4 * min(q, S)), the update (sampled
+    ids, count in/out, appended ids) and the outputs (draft + num_valid).
+    Returns [NREP, DECODE_STEPS]."""
+    q0 = data["num_tokens"].astype(np.int64)
+    samp = data["sampled"]
+    out = np.zeros((NREP, DECODE_STEPS))
+    for r in range(NREP):
+        q = np.roll(q0, rep_shift * r)
+        for j in range(DECODE_STEPS):
+            sj = np.roll(samp[j], rep_shift * r, axis=0)
+            cnt = (sj != -1).sum(axis=1)
+            qn = q + cnt
+            mask = (cnt > 0) & (qn < S)
+            read = 4 * np.minimum(qn, S)[mask].sum()
+            upd = (4 * T + 8 + 4 * cnt).sum()
+            outb = B * (4 * K + 4)
+            out[r, j] = read + upd + outb
+            q = qn
+    return out
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 f"--query-gpu={self.FIELDS}", "--format=csv,noheader",
+                 "-lms", "50"], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.15)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["n/a"]}
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        mhz, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                 "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                mhz.append(float(parts[0].split()[0]))
+                mx = float(parts[1].split()[0])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[3:7]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None,
+                "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from suffixgpu_b200 import SuffixGPUDrafter
+    from suffixgpu_b200 import workloads as wl
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev,
+                                timeout=datetime.timedelta(seconds=120))
+
+    data = workload(rank)
+    shift = 7
+    drafter = SuffixGPUDrafter(device=dev, **wl.CONFIG2_DRAFTER)
+    tok0 = torch.from_numpy(data["token_ids"]).to(dev)
+    q0 = torch.from_numpy(data["num_tokens"]).to(dev)
+    samp0 = torch.from_numpy(data["sampled"]).to(dev)  # [100, B, T]
+    reps = []
+    for r in range(NREP):
+        tok = torch.roll(tok0, shifts=shift * r, dims=0).contiguous()
+        cnt0 = torch.roll(q0, shifts=shift * r, dims=0).contiguous()
+        samp = torch.roll(samp0, shifts=shift * r, dims=1).contiguous()
+        reps.append({"tok": tok, "cnt0": cnt0, "samp": samp})
+    alg = algorithmic_bytes(data, shift)  # [NREP, 100]
+
+    def step_seq(n):
+        """(replica, decode step) of bench steps 0..n-1."""
+        return [(i % NREP, (i // NREP) % DECODE_STEPS) for i in range(n)]
+
+    cycle = NREP * DECODE_STEPS
+
+    def run_seq(seq):
+        """Each replica starts from its initial counts and chains the
+        counts every call returns, so a sequence is self-contained (no
+        copies between calls: one kernel launch per step)."""
+        cur = [rp["cnt0"] for rp in reps]
+        for (r, j) in seq:
+            rp = reps[r]
+            if j == 0:
+                cur[r] = rp["cnt0"]
+            _, _, cur[r] = drafter.propose_with_update(
+                cur[r], rp["tok"], rp["samp"][j])
+
+    def capture(seq):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            run_seq(seq)
+        return g
+
+    # warm-up: eager calls (exercise the API), then the graphs once
+    run_seq(step_seq(max(args.warmup, 3)))
+    torch.cuda.synchronize()
+    full = capture(step_seq(cycle)) if args.steps >= cycle else None
+    rem = args.steps % cycle
+    part = capture(step_seq(rem)) if rem else None
+    for g in (full, part):
+        if g is not None:
+            g.replay()
+    torch.cuda.synchronize()
+
+    # count our kernel launches per step (one fused launch per call)
+    launches = args.steps  # one sg_local_draft per propose_with_update
+
+    clock = ClockSampler(local)
+    clock.start()
+    stream = torch.cuda.current_stream()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps // cycle):
+        full.replay()
+    if part is not None:
+        part.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = clock.stop()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+
+    # algorithmic bytes over the timed steps (the reset node is outside)
+    seq = step_seq(args.steps)
+    alg_total = float(sum(alg[r, j] for (r, j) in seq))
+    per_launch_ms = ms / args.steps
+    achieved = alg_total / args.steps / (per_launch_ms * 1e-3) / 1e9
+    peaks = _peaks()
+    rows_total = world * B * args.steps
+
+    # end-to-end through the public API with host buffers
+    e2e = None if args.no_e2e else run_e2e(args, drafter, reps, data, dev,
+                                           world)
+
+    res = None
+    if rank == 0:
+        res = {
+            "metric": METRIC,
+            "value": rows_total / (ms_max * 1e-3),
+            "unit": "rows/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "int32",
+            "data": "synthetic (seeded copy/Zipf rows, BASELINE config 2)",
+            "config": dict(CONFIG, parallelism=f"dp{world}"),
+            "impl": "ours",
+            "gpu_launches": launches,
+            "e2e": e2e,
+            "roofline": {
+                "bound": "hbm",
+                "kernel": "local_draft_kernel",
+                "achieved": achieved,
+                "peak": peaks["hbm_gbs"],
+                "peak_source": peaks["source"],
+                "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"],
+                "traffic": _traffic(),
+                "alg_bytes_per_launch": alg_total / args.steps,
+                "launch_us": per_launch_ms * 1e3,
+            },
+            "clocks": clocks,
+        }
+        res["cpu_baseline"] = None if (args.no_cpu or world > 1) \
+            else cpu_baseline(args, data)
+    if world > 1:
+        dist.barrier()
+        del full, part
+        dist.destroy_process_group()
+    return res
+
+
+def run_e2e(args, drafter, reps, data, dev, world):
+    """Same metric through the public API: per step an H2D copy of the
+    step's sampled ids from pinned host memory, the eager
+    propose_with_update call, and a D2H read of draft + num_valid."""
+    import torch
+    import torch.distributed as dist
+    n = args.e2e_steps
+    samp_host = [torch.from_numpy(np.roll(data["sampled"], 7 * r, axis=1))
+                 .pin_memory() for r in range(NREP)]
+    samp_dev = torch.empty(B, T, dtype=torch.int32, device=dev)
+    out_draft = torch.empty(B, K, dtype=torch.int32).pin_memory()
+    out_nv = torch.empty(B, dtype=torch.int32).pin_memory()
+    seq = [(i % NREP, (i // NREP) % DECODE_STEPS) for i in range(n + 3)]
+    cur = [rp["cnt0"] for rp in reps]
+
+    def one(r, j):
+        rp = reps[r]
+        if j == 0:
+            cur[r] = rp["cnt0"]
+        samp_dev.copy_(samp_host[r][j], non_blocking=True)
+        d, nv, cur[r] = drafter.propose_with_update(cur[r], rp["tok"],
+                                                    samp_dev)
+        out_draft.copy_(d, non_blocking=True)
+        out_nv.copy_(nv, non_blocking=True)
+
+    for (r, j) in seq[:3]:  # warm-up
+        one(r, j)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for (r, j) in seq[3:]:
+        one(r, j)
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    tt = torch.tensor([dt], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    dt = float(tt.item())
+    return {"value": world * B * n / dt, "unit": "rows/s",
+            "h2d_bytes_per_step": B * T * 4,
+            "d2h_bytes_per_step": B * K * 4 + B * 4,
+            "steps": n, "mode": "eager public API, pinned host buffers"}
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            pk = json.load(f)
+        return {"hbm_gbs": float(pk["hbm_gbs"]), "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def _traffic():
+    """DRAM bytes per launch of the kernel from the committed ncu summary
+    (profiles/local_draft_config2.txt), or None."""
+    path = os.path.join(ROOT, "profiles", "local_draft_config2.txt")
+    try:
+        for ln in open(path):
+            if ln.startswith("traffic_bytes_per_launch:"):
+                return float(ln.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle port of the reference's torch CPU path)
+# ---------------------------------------------------------------------------
+def _cpu_chunk(payload):
+    rows, steps, cfg = payload
+    sys.path.insert(0, ROOT)
+    from oracle import suffix_oracle as so
+    tok, q, samp = rows
+    d = so.SuffixDrafter(**cfg)
+    t0 = time.perf_counter()
+    for j in range(steps):
+        _, _, q = d.propose_with_update(q, tok, samp[j])
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(args, data, cores=None) -> dict:
+    """Reference algorithm (numpy port) on a bounded sample: cpu_rows rows
+    of config 2 for cpu_steps decode steps, rows split across one process
+    per host core (rows are independent). Each worker times its own
+    compute; the sample's time is the slowest worker's."""
+    import multiprocessing as mp
+    from concurrent.futures import ProcessPoolExecutor
+    cores = cores or max(1, os.cpu_count() or 1)
+    rows = min(args.cpu_rows, B)
+    steps = args.cpu_steps
+    tok = data["token_ids"][:rows].copy()
+    q = data["num_tokens"][:rows].copy()
+    samp = data["sampled"][:steps, :rows].copy()
+    nproc = min(cores, rows)
+    bounds = np.linspace(0, rows, nproc + 1).astype(int)
+    from suffixgpu_b200.workloads import CONFIG2_DRAFTER
+    chunks = [((tok[a:b_].copy(), q[a:b_].copy(), samp[:, a:b_].copy()),
+               steps, dict(CONFIG2_DRAFTER))
+              for a, b_ in zip(bounds[:-1], bounds[1:]) if b_ > a]
+    t0 = time.perf_counter()
+    with ProcessPoolExecutor(max_workers=len(chunks),
+                             mp_context=mp.get_context("spawn")) as ex:
+        times = list(ex.map(_cpu_chunk, chunks))
+    wall = time.perf_counter() - t0
+    slowest = max(times)
+    return {"value": rows * steps / slowest, "unit": "rows/s",
+            "cores": len(chunks), "kind": "port",
+            "sample": f"{rows} rows of config 2 x {steps} decode steps, "
+                      f"numpy restatement of the reference CPU path, "
+                      f"{len(chunks)} worker processes; slowest worker "
+                      f"{slowest:.2f} s compute, {wall:.2f} s wall with "
+                      f"start-up"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    data = workload(0)
+    cb = cpu_baseline(args, data)
+    v = cb["value"]
+    return {
+        "metric": METRIC, "value": v, "unit": "rows/s", "n_gpus": 0,
+        "steps": args.cpu_steps, "warmup": 0,
+        "ms_per_step": 1e3 * min(args.cpu_rows, B) / v,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int32",
+        "data": "synthetic (seeded copy/Zipf rows, BASELINE config 2)",
+        "config": dict(CONFIG, parallelism="host cores"),
+        "impl": "reference", "cpu_baseline": cb,
+        "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        res = run_reference(args)
+    else:
+        res = run_ours(args)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,157 @@
+/*
+ * suffixgpu.h -- C ABI of the B200 (sm_100a) SuffixGPU drafter kernels.
+ *
+ * Every entry point takes raw device pointers, sizes and scalars plus a
+ * cudaStream_t, enqueues work on that stream and returns a status code.
+ * None of them allocates device memory or synchronises the host, so they
+ * can be captured into CUDA graphs. Scratch memory, where a kernel needs
+ * some, is passed in by the caller as a workspace pointer + byte size; the
+ * matching *_workspace_size() query says how much.
+ *
+ * Integer conventions: token ids are int32. Where the reference's Python
+ * operator returns int64 tensors (counts, positions, SA intervals), the
+ * corresponding pointer here is int64_t so the host can hand the buffer
+ * back without a conversion.
+ *
+ * Reference = zip95297/SuffixGPU (Python/Triton). Each declaration names the
+ * reference function whose results it reproduces.
+ */
+#ifndef SUFFIXGPU_H_
+#define SUFFIXGPU_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* sg_stream_t; /* == cudaStream_t */
+
+/* ---- status codes ------------------------------------------------------ */
+#define SG_OK 0
+#define SG_ERR_INVALID 1     /* bad shape, pointer or parameter */
+#define SG_ERR_WORKSPACE 2   /* workspace missing or too small */
+#define SG_ERR_CUDA 3        /* launch / runtime error (see sg_last_cuda_error) */
+#define SG_ERR_UNSUPPORTED 4 /* shape beyond this build's limits */
+
+/* Human-readable text for a status code (static storage). */
+const char* sg_status_string(int status);
+/* Last CUDA error code seen by an entry point on this thread (0 if none). */
+int sg_last_cuda_error(void);
+/* ABI version: (major << 16) | minor. */
+int sg_abi_version(void);
+
+/* ---- local drafter ------------------------------------------------------
+ * Drafter parameters shared by the local and global paths
+ * (reference: suffix_gpu/proposer.py:37-112, local_matcher.py:52-74).
+ */
+typedef struct sg_draft_params {
+  int32_t batch;            /* B: rows */
+  int32_t seq_len;          /* S: row capacity of token_ids */
+  int64_t row_stride;       /* elements between consecutive rows (>= S) */
+  int32_t k;                /* draft length K (<= 64) */
+  int32_t max_pattern_len;  /* P (<= 255) */
+  int32_t max_occurrences;  /* R (<= 1024) */
+  int32_t num_backoff;      /* C: support thresholds 2^0..2^(C-1) (<= 32) */
+  int32_t min_match_len;    /* clamped to >= 1 like the reference */
+  int32_t has_spec_factor;  /* 0: cap = K; 1: floor(f*L + o) */
+  float spec_factor;        /* max_spec_factor (rounded to fp32) */
+  float spec_offset;        /* max_spec_offset (rounded to fp32) */
+  float min_token_prob;     /* rounded to fp32 */
+  float vote_alpha;         /* vote_smoothing_alpha (rounded to fp32) */
+} sg_draft_params;
+
+/* Inputs of one local draft step. */
+typedef struct sg_local_inputs {
+  const int32_t* num_tokens; /* [B] counts before the update (propose mode:
+                                the current counts) */
+  int32_t* token_ids;        /* [B, row_stride] resident buffer; updated in
+                                place in update mode */
+  const int32_t* sampled;    /* [B, sampled_cols] ids, -1 padded; NULL =
+                                propose mode (no update) */
+  int32_t sampled_cols;      /* T */
+  const int32_t* valid_count; /* [B] or NULL: #(sampled[b, :] != -1) */
+  const uint8_t* mask;       /* propose mode: [B] rows allowed to draft, or
+                                NULL = all rows */
+  int64_t limit;             /* update mode: rows draft only while
+                                new_count < limit (min(max_model_len, S)) */
+} sg_local_inputs;
+
+/* Outputs of one local draft step (optional ones may be NULL). */
+typedef struct sg_local_outputs {
+  int32_t* draft;       /* [B, K] int32, -1 past num_valid */
+  int32_t* num_valid;   /* [B] int32 */
+  int32_t* new_counts;  /* [B] int32, update mode only */
+  float* best_score;    /* [B] score of the selected local candidate */
+  int32_t* best_len;    /* [B] its match length */
+  int32_t* best_occ;    /* [B] its occurrence count */
+  uint8_t* row_mask;    /* [B] 1 where the row was allowed to draft */
+} sg_local_outputs;
+
+/*
+ * Fused local draft step: optional scatter-append of the sampled ids,
+ * eligibility mask, local suffix match with backoff candidates, earliest
+ * occurrences, continuation vote/score and best-candidate select.
+ *
+ * Replaces SuffixGPUDrafter.propose_with_update / propose for the
+ * local-only drafter (suffix_gpu/proposer.py:135-218, :220-331 with
+ * global_index None), i.e. LocalMatchKernel.forward
+ * (suffix_gpu/local_matcher.py:83-242) and the Triton kernels
+ * _scatter_append_kernel / _match_back_kernel / _first_occ_kernel /
+ * _expand_chain_kernel_v2 (suffix_gpu/triton_kernels.py:39-256).
+ *
+ * Update mode (sampled != NULL): token_ids rows are updated in place,
+ * new_counts[b] = num_tokens[b] + cnt[b] with cnt = valid_count[b] or the
+ * number of sampled[b, :] entries != -1, and a row drafts only when
+ * cnt > 0 and new_count < limit (proposer.py:186-218).
+ * Propose mode (sampled == NULL): counts are num_tokens and rows draft
+ * where mask[b] != 0.
+ * Rows must fit in shared memory: S <= ~40k tokens on B200.
+ */
+int sg_local_draft(const sg_draft_params* params, const sg_local_inputs* in,
+                   const sg_local_outputs* out, sg_stream_t stream);
+
+/* ---- reference operator layer (suffix_gpu/triton_kernels.py) ----------- */
+
+/* scatter_append (triton_kernels.py:392-402 / proposer.py:166-188):
+ * token_ids[b, base[b] + j] = sampled[b, j] for j < min(T, cnt[b]) when
+ * sampled != -1 and the position is < S. new_counts = base + cnt.
+ * valid_count NULL: cnt = #(sampled[b, :] != -1). */
+int sg_scatter_append(int32_t* token_ids, int64_t row_stride, int32_t batch,
+                      int32_t seq_len, const int32_t* base,
+                      const int32_t* valid_count, const int32_t* sampled,
+                      int32_t sampled_cols, int32_t* new_counts,
+                      sg_stream_t stream);
+
+/* match_back (triton_kernels.py:259-281): out[b, i] = longest L <= P with
+ * src[.., i-L:i] == the newest-first pattern pat[b, :L]; positions before
+ * the buffer start read -1. row_stride 0 = one shared src of n_src
+ * elements; otherwise src is [B, row_stride]. out is [B, n_out] int32. */
+int sg_match_back(const int32_t* src, int64_t row_stride, int64_t n_src,
+                  const int32_t* pat, int32_t batch, int32_t pat_len,
+                  int64_t n_out, int32_t* out, sg_stream_t stream);
+
+/* first_occurrences (triton_kernels.py:362-389): for each row of B*C
+ * (row / C selects the mb row), the earliest R positions with
+ * mb >= thr (thr <= 0: none), zero-padded, count clamped to R. */
+int sg_first_occurrences(const int32_t* mb, int64_t n_cols,
+                         const int64_t* thr, int32_t rows, int32_t cands,
+                         int32_t max_occ, int64_t* out_pos,
+                         int64_t* out_cnt, sg_stream_t stream);
+
+/* expand_chain (suffix_gpu/expand.py:59-147, triton_kernels.py:305-338),
+ * unweighted votes: cont [N, R, K] int32 (-1 = no token), num_occ [N],
+ * cap [N] (NULL = K). Outputs chain [N, K] int32, num_valid [N] int64,
+ * num_emit [N] int64, score [N] fp32. */
+int sg_expand_chain(const int32_t* cont, int32_t rows, int32_t max_occ,
+                    int32_t k, const int64_t* num_occ, const int64_t* cap,
+                    float min_token_prob, float alpha, int32_t* chain,
+                    int64_t* num_valid, int64_t* num_emit, float* score,
+                    sg_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SUFFIXGPU_H_ */

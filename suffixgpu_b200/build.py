@@ -1,0 +1,80 @@
+"""Build the sm_100a kernel library in-tree with nvcc.
+
+``python -m suffixgpu_b200.build`` compiles every ``csrc/*.cu`` for
+``sm_100a`` (``-gencode arch=compute_100a,code=sm_100a``) into
+``suffixgpu_b200/libsuffixgpu_b200.so``. Objects are rebuilt only when a
+source or header is newer. The library has no torch dependency: it exports
+the C ABI declared in ``include/suffixgpu.h``.
+"""
+
+from __future__ import annotations
+
+import glob
+import os
+import shutil
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+CSRC = os.path.join(PKG, "csrc")
+OBJ = os.path.join(PKG, "_build")
+LIB = os.path.join(PKG, "libsuffixgpu_b200.so")
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
+         "-fmad=false", "--expt-relaxed-constexpr",
+         "-I" + os.path.join(ROOT, "include")]
+
+
+def _nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"),
+                 "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def _newest_dep() -> float:
+    deps = glob.glob(os.path.join(CSRC, "*.cuh")) + [
+        os.path.join(ROOT, "include", "suffixgpu.h")]
+    return max(os.path.getmtime(p) for p in deps)
+
+
+def build(verbose: bool = False, extra_flags: list[str] | None = None) -> str:
+    """Compile (incrementally) and link; returns the library path."""
+    nvcc = _nvcc()
+    os.makedirs(OBJ, exist_ok=True)
+    srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    dep_t = _newest_dep()
+    flags = FLAGS + (extra_flags or [])
+    jobs = []
+    objs = []
+    for src in srcs:
+        obj = os.path.join(OBJ, os.path.basename(src)[:-3] + ".o")
+        objs.append(obj)
+        if (not os.path.exists(obj)
+                or os.path.getmtime(obj) < max(os.path.getmtime(src), dep_t)):
+            jobs.append([nvcc, *ARCH, *flags, "-c", src, "-o", obj])
+
+    def run(cmd):
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed:\n{' '.join(cmd)}\n{r.stderr}")
+        if verbose and r.stderr.strip():
+            print(r.stderr, file=sys.stderr)
+        return r
+
+    with ThreadPoolExecutor(max_workers=min(8, max(1, len(jobs)))) as ex:
+        list(ex.map(run, jobs))
+    if jobs or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(
+            os.path.getmtime(o) for o in objs):
+        run([nvcc, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"])
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(verbose="-v" in sys.argv))

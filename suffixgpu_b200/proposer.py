@@ -1,0 +1,185 @@
+"""SuffixGPUDrafter: the reference drafter API (suffix_gpu/proposer.py:26-393)
+on the sm_100a kernels.
+
+The local-only drafter is one fused kernel launch per propose /
+propose_with_update call (``sg_local_draft``), with no host sync, so the
+call can be captured into a CUDA graph. With ``enable_global=True`` the
+global index (corpus suffix array + delta buffer) adds the SA search, the
+delta scan and the global candidate expansion, combined with the local
+winner by the reference's strict-greater rule.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from suffixgpu_b200 import ops
+from suffixgpu_b200.local_matcher import LocalMatchKernel
+
+
+def global_caps(max_pattern_len: int, num_backoff: int) -> list[int]:
+    """Descending global length caps (proposer.py:78-87)."""
+    if num_backoff == 1:
+        caps = [max_pattern_len]
+    else:
+        caps = [max(2, max_pattern_len >> i)
+                for i in range(num_backoff - 1)] + [2]
+    return sorted(set(caps), reverse=True)
+
+
+class SuffixGPUDrafter:
+    """Device-resident suffix-decoding drafter (device tensors in and out,
+    no host synchronization on the propose path)."""
+
+    def __init__(
+        self,
+        k: int,
+        device: torch.device | str = "cuda",
+        max_pattern_len: int = 32,
+        min_match_len: int = 1,
+        max_occurrences: int = 128,
+        enable_global: bool = False,
+        global_capacity: int = 1 << 22,
+        delta_capacity: int = 1 << 16,
+        rebuild_threshold: int | None = None,
+        rebuild_stream: torch.cuda.Stream | None = None,
+        max_spec_factor: float | None = None,
+        max_spec_offset: float = 0.0,
+        min_token_prob: float = 0.0,
+        num_backoff: int = 8,
+        vote_smoothing_alpha: float = 0.0,
+        parallel_paths: bool = True,
+    ):
+        self.k = k
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("SuffixGPUDrafter (suffixgpu_b200) runs on CUDA "
+                             f"devices only, got {self.device}")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.max_pattern_len = max_pattern_len
+        self.max_spec_factor = max_spec_factor
+        self.max_spec_offset = max_spec_offset
+        self.min_token_prob = min_token_prob
+        self.num_backoff = max(1, int(num_backoff))
+        self.vote_smoothing_alpha = float(vote_smoothing_alpha)
+        self.parallel_paths = bool(parallel_paths)
+        support_thresholds = tuple(2 ** i for i in range(self.num_backoff))
+        caps = global_caps(max_pattern_len, self.num_backoff)
+        self._global_caps = torch.tensor(caps, dtype=torch.int64,
+                                         device=self.device)
+        self.local_kernel = LocalMatchKernel(
+            k=k, max_pattern_len=max_pattern_len,
+            min_match_len=min_match_len, max_occurrences=max_occurrences,
+            min_token_prob=min_token_prob, max_spec_factor=max_spec_factor,
+            max_spec_offset=max_spec_offset,
+            support_thresholds=support_thresholds,
+            vote_smoothing_alpha=self.vote_smoothing_alpha)
+        self.global_index = None
+        self._ingested: dict = {}
+        if enable_global:
+            from suffixgpu_b200.global_index import GlobalIndex
+            self.global_index = GlobalIndex(
+                capacity=global_capacity, delta_capacity=delta_capacity,
+                k=k, max_occurrences=max_occurrences,
+                rebuild_threshold=rebuild_threshold, device=self.device,
+                rebuild_stream=rebuild_stream)
+
+    # ------------------------------------------------------------------
+    def poll(self) -> None:
+        """Host-side: swap in a finished background rebuild, if any."""
+        if self.global_index is not None:
+            self.global_index.poll_rebuild()
+
+    def update_state(self, num_tokens_no_spec: torch.Tensor,
+                     token_ids_gpu: torch.Tensor,
+                     sampled_token_ids: torch.Tensor,
+                     valid_sampled_tokens_count: torch.Tensor | None = None
+                     ) -> torch.Tensor:
+        """Scatter the sampled ids into the resident buffer (in place) and
+        return the updated counts [B] int32 (proposer.py:135-184)."""
+        return ops.scatter_append(token_ids_gpu, num_tokens_no_spec,
+                                  valid_sampled_tokens_count,
+                                  sampled_token_ids)
+
+    def propose_with_update(
+        self,
+        num_tokens_no_spec: torch.Tensor,
+        token_ids_gpu: torch.Tensor,
+        sampled_token_ids: torch.Tensor,
+        valid_sampled_tokens_count: torch.Tensor | None = None,
+        max_model_len: int | None = None,
+    ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """update_state + eligibility mask + propose, all on device
+        (proposer.py:186-214). Returns (draft [B,k] int32, num_valid [B]
+        int32, new_num_tokens [B] int32)."""
+        s = token_ids_gpu.shape[1]
+        limit = s if max_model_len is None else min(max_model_len, s)
+        if self.global_index is None:
+            o = self.local_kernel.run(
+                num_tokens_no_spec, token_ids_gpu,
+                sampled=sampled_token_ids,
+                valid_count=valid_sampled_tokens_count, limit=limit)
+            return o["draft"], o["num_valid"], o["new_counts"]
+        o = self.local_kernel.run(
+            num_tokens_no_spec, token_ids_gpu, sampled=sampled_token_ids,
+            valid_count=valid_sampled_tokens_count, limit=limit,
+            extras=True)
+        draft, nv = self._global_step(o["new_counts"], token_ids_gpu, o)
+        return draft, nv, o["new_counts"]
+
+    def propose(self, num_tokens_no_spec: torch.Tensor,
+                token_ids_gpu: torch.Tensor,
+                combined_mask: torch.Tensor | None = None
+                ) -> tuple[torch.Tensor, torch.Tensor]:
+        """Draft from local history (and the global index when enabled)
+        (proposer.py:216-327). Returns (draft [B,k] int32, num_valid [B]
+        int32)."""
+        if self.global_index is None:
+            o = self.local_kernel.run(num_tokens_no_spec, token_ids_gpu,
+                                      mask=combined_mask)
+            return o["draft"], o["num_valid"]
+        o = self.local_kernel.run(num_tokens_no_spec, token_ids_gpu,
+                                  mask=combined_mask, extras=True)
+        return self._global_step(num_tokens_no_spec, token_ids_gpu, o)
+
+    def _global_step(self, counts, token_ids, local):
+        return self.global_index.propose_combine(
+            counts, token_ids, local, self)
+
+    # ------------------------------------------------------------------
+    # host-side ingestion (proposer.py:329-390)
+    # ------------------------------------------------------------------
+    def harvest_finished(self, row_indices: list[int], lengths: list[int],
+                         token_ids_gpu: torch.Tensor) -> None:
+        rows = [token_ids_gpu[r] for r in row_indices]
+        self.harvest_rows(rows, lengths)
+
+    def harvest_rows(self, rows: list[torch.Tensor],
+                     lengths: list[int]) -> None:
+        if self.global_index is None or not rows:
+            return
+        docs = [row[:ln] for row, ln in zip(rows, lengths) if ln > 0]
+        if docs:
+            self.global_index.append_documents(docs)
+
+    def ingest_active(self, keys: list, rows: list[torch.Tensor],
+                      lengths: list[int], final: bool = False,
+                      chunk: int = 64) -> None:
+        if self.global_index is None:
+            return
+        overlap = self.max_pattern_len + self.k
+        docs = []
+        for key, row, ln in zip(keys, rows, lengths):
+            done = self._ingested.get(key, 0)
+            if ln - done >= chunk or (final and ln > done):
+                start = max(0, done - overlap)
+                docs.append(row[start:ln])
+                self._ingested[key] = ln
+            if final:
+                self._ingested.pop(key, None)
+        if docs:
+            self.global_index.append_documents(docs)
+
+    def load_model(self, *args, **kwargs) -> None:
+        pass

@@ -1,0 +1,77 @@
+"""C ABI checks that need no GPU: the in-tree library builds for sm_100a,
+loads, and exports every entry point include/suffixgpu.h declares."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "suffixgpu.h")
+
+
+def declared_symbols() -> list[str]:
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(sg_\w+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def libpath():
+    from suffixgpu_b200 import build
+    return build.build()
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    assert "sg_local_draft" in syms
+    assert len(syms) >= 6
+
+
+def test_library_exports_every_declared_symbol(libpath):
+    lib = ctypes.CDLL(libpath)
+    missing = [s for s in declared_symbols() if not hasattr(lib, s)]
+    assert not missing, f"missing exports: {missing}"
+
+
+def test_status_strings_and_version(libpath):
+    from suffixgpu_b200 import _lib
+    L = _lib.lib()
+    assert L.sg_abi_version() >> 16 == 1
+    assert L.sg_status_string(0).decode() == "ok"
+    assert "invalid" in L.sg_status_string(1).decode()
+
+
+def test_ctypes_struct_layout_matches_header():
+    from suffixgpu_b200._lib import DraftParams, LocalInputs, LocalOutputs
+    # field order/sizes of include/suffixgpu.h on LP64
+    assert ctypes.sizeof(DraftParams) == 56
+    assert DraftParams.row_stride.offset == 8
+    assert DraftParams.vote_alpha.offset == 52
+    assert ctypes.sizeof(LocalInputs) == 56
+    assert LocalInputs.limit.offset == 48
+    assert ctypes.sizeof(LocalOutputs) == 56
+
+
+def test_invalid_arguments_rejected_without_gpu(libpath):
+    """Argument validation runs on the host before any CUDA call."""
+    from suffixgpu_b200._lib import DraftParams, LocalInputs, LocalOutputs
+    from suffixgpu_b200 import _lib
+    L = _lib.lib()
+    p = DraftParams(batch=2, seq_len=16, row_stride=16, k=0,
+                    max_pattern_len=8, max_occurrences=8, num_backoff=3,
+                    min_match_len=1)
+    st = L.sg_local_draft(ctypes.byref(p), ctypes.byref(LocalInputs()),
+                          ctypes.byref(LocalOutputs()), None)
+    assert st == 1  # k = 0
+    p.k = 4
+    p.batch = 0
+    st = L.sg_local_draft(ctypes.byref(p), ctypes.byref(LocalInputs()),
+                          ctypes.byref(LocalOutputs()), None)
+    assert st == 0  # empty batch: nothing to do
+    assert L.sg_expand_chain(None, 1, 0, 4, None, None, 0.0, 0.0, None, None,
+                             None, None, None) == 1
