@@ -7,25 +7,27 @@
 // [B,S], the occurrence lists and the [B,C,R,K] continuation block in HBM;
 // here a single kernel keeps everything for a row in shared memory:
 //
-//   1. TMA bulk copy (cp.async.bulk + mbarrier) of the row's committed
-//      tokens into shared memory; the sampled ids are scattered into both
-//      the shared copy and the HBM buffer (update_state semantics).
-//   2. match_back for every end position i < q, stored as bytes, with a
-//      (P+1)-bin histogram of the values (the reference's topk over [B,S]
-//      becomes a suffix sum over the histogram: the t-th largest value is
-//      the largest L with #{mb >= L} >= t).
-//   3. Earliest occurrences of every candidate in one ordered block-wide
-//      compaction (two passes over the byte array).
-//   4. One warp per candidate expands its continuation chain (sg_vote.cuh),
-//      reading continuations straight from the shared row.
-//   5. argmax(score + f32(cand) * 1e-6) and the masked draft write.
+//   1. Warp 0 reads the row's count and sampled ids; one thread issues a
+//      TMA bulk copy (cp.async.bulk + mbarrier) of the committed tokens into
+//      shared memory; the sampled ids are then scattered into both the
+//      shared copy and the HBM buffer (update_state semantics).
+//   2. match_back for every end position i < q. Each warp owns a contiguous
+//      segment of positions and appends the nonzero ones, in position order,
+//      to its own hit list (ballot prefix sums, no block-wide scan); a
+//      (P+1)-bin histogram of the values is kept with warp-aggregated
+//      atomics. The reference's topk over [B,S] becomes a count over the
+//      histogram: the t-th largest value is the largest L with
+//      #{mb >= L} >= t.
+//   3. One warp per candidate walks the hit lists in order (32 entries per
+//      ballot) to collect its earliest R occurrences, then expands its
+//      continuation chain (sg_vote.cuh) reading continuations straight from
+//      the shared row, stopping at the candidate's spec cap.
+//   4. argmax(score + f32(cand) * 1e-6) and the masked draft write.
 //
 // HBM traffic per row: the committed tokens once, the sampled ids, the
 // appended tokens, and the outputs.
 
 #include <cuda_runtime.h>
-
-#include <algorithm>
 
 #include "sg_common.cuh"
 #include "sg_vote.cuh"
@@ -35,12 +37,13 @@ namespace sg {
 constexpr int kLocalThreads = 256;
 constexpr int kLocalWarps = kLocalThreads / 32;
 constexpr int kMaxCand = 16;  // candidates with threshold 2^c <= S (S < 2^16)
+constexpr int kWalkHits = 256;  // rows with at most this many hits: walk
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 
 struct LocalLayout {
-  size_t off_tok, off_mb, off_pat, off_hist, off_cand, off_cnt, off_occ;
-  size_t off_score, off_emit, off_chain, off_scan, off_warp, warp_bytes;
+  size_t off_tok, off_hits, off_pat, off_hist, off_cand, off_score, off_emit;
+  size_t off_chain, off_wlen, off_wcnt, off_occ, off_warp, warp_bytes;
   size_t total;
   int H;
   __host__ __device__ LocalLayout(int S, int P, int C, int R, int K) {
@@ -48,17 +51,19 @@ struct LocalLayout {
     H = static_cast<int>(next_pow2_u32(static_cast<uint32_t>(2 * R > 64 ? 2 * R : 64)));
     size_t o = 16;  // mbarrier
     off_tok = o;   o = align16(o + 4 * s4);
-    off_mb = o;    o = align16(o + s4);
+    // per-warp hit lists: segments are rounded up to 128 positions each
+    off_hits = o;  o = align16(o + 4 * s4 + 4 * 128 * kLocalWarps);
     off_pat = o;   o = align16(o + 4 * static_cast<size_t>(P));
     off_hist = o;  o = align16(o + 4 * static_cast<size_t>(P + 2));
     off_cand = o;  o = align16(o + 4 * kMaxCand);
-    off_cnt = o;   o = align16(o + 4 * kMaxCand);
-    off_occ = o;   o = align16(o + 4 * static_cast<size_t>(C) * R);
     off_score = o; o = align16(o + 4 * kMaxCand);
     off_emit = o;  o = align16(o + 4 * kMaxCand);
     off_chain = o; o = align16(o + 4 * static_cast<size_t>(C) * K);
-    off_scan = o;  o = align16(o + 4 * static_cast<size_t>(kLocalWarps) * kMaxCand);
-    warp_bytes = align16(4 * static_cast<size_t>(R) + 8 * static_cast<size_t>(H));
+    off_wlen = o;  o = align16(o + 8 * kLocalWarps);  // lengths + max mb
+    off_wcnt = o;  o = align16(o + 4 * static_cast<size_t>(kLocalWarps) * kMaxCand);
+    off_occ = o;   o = align16(o + 4 * static_cast<size_t>(C) * R);
+    warp_bytes = align16(4 * static_cast<size_t>(R > 64 ? R : 64) +
+                         8 * static_cast<size_t>(H));
     off_warp = o;  o += kLocalWarps * warp_bytes;
     total = o;
   }
@@ -80,8 +85,43 @@ __device__ __forceinline__ long long spec_cap(const sg_draft_params& p,
   return c > 0 ? c : 0;
 }
 
-template <int RJ>
-__global__ void __launch_bounds__(kLocalThreads)
+// Candidate lengths for support thresholds 2^0..2^(C-1), from the
+// histogram of match_back values (local_matcher.py:134-157): cand_t is the
+// t-th largest mb, i.e. the largest L with #{mb >= L} >= t (0 if none),
+// zeroed below min_match_len and when equal to the previous candidate.
+// Executed by a full warp; lane c < C returns candidate c.
+__device__ __forceinline__ int warp_candidates(const int* hist, int P, int C,
+                                               int min_match) {
+  const int lane = lane_id();
+  int cand = 0;
+  int carry = 0;  // #{mb > top length of the current chunk}
+  const int nchunk = (P + 31) / 32;
+  for (int ch = nchunk - 1; ch >= 0; --ch) {
+    const int L = ch * 32 + 1 + lane;  // lengths 32ch+1 .. 32ch+32
+    int v = L <= P ? hist[L] : 0;
+    // suffix sum within the chunk: sum over lanes >= lane
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_down_sync(SG_FULL_MASK, v, o);
+      if (lane + o < 32) v += u;
+    }
+    const int cnt_ge = v + carry;
+    carry += __shfl_sync(SG_FULL_MASK, v, 0);
+    // cand_c = #{L : cnt_ge[L] >= 2^c}: cnt_ge is non-increasing in L
+    for (int c = 0; c < C; ++c) {
+      const unsigned m =
+          __ballot_sync(SG_FULL_MASK, L <= P && cnt_ge >= (1ll << c));
+      if (lane == c) cand += __popc(m);
+    }
+  }
+  const int mml = min_match > 1 ? min_match : 1;
+  if (cand < mml) cand = 0;
+  const int prev = __shfl_up_sync(SG_FULL_MASK, cand, 1);
+  return (lane > 0 && prev == cand) ? 0 : cand;
+}
+
+template <int RJ, int NC>
+__global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
     local_draft_kernel(const LocalArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   const sg_draft_params& p = a.p;
@@ -90,69 +130,92 @@ __global__ void __launch_bounds__(kLocalThreads)
   const LocalLayout L(S, P, C, R, K);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
   int* tok_s = reinterpret_cast<int*>(smem + L.off_tok);
-  uint8_t* mb_s = smem + L.off_mb;
+  int* hits = reinterpret_cast<int*>(smem + L.off_hits);
   int* pat = reinterpret_cast<int*>(smem + L.off_pat);
   int* hist = reinterpret_cast<int*>(smem + L.off_hist);
-  int* cand_s = reinterpret_cast<int*>(smem + L.off_cand);
-  int* cnt_s = reinterpret_cast<int*>(smem + L.off_cnt);
-  int* occ_s = reinterpret_cast<int*>(smem + L.off_occ);
   float* score_s = reinterpret_cast<float*>(smem + L.off_score);
   int* emit_s = reinterpret_cast<int*>(smem + L.off_emit);
+  int* cand_s = reinterpret_cast<int*>(smem + L.off_cand);
   int* chain_s = reinterpret_cast<int*>(smem + L.off_chain);
-  int* scan_s = reinterpret_cast<int*>(smem + L.off_scan);
+  int* wlen = reinterpret_cast<int*>(smem + L.off_wlen);
+  int* wmax = wlen + kLocalWarps;
+  int* wcnt = reinterpret_cast<int*>(smem + L.off_wcnt);  // [warps][cands]
+  int* occ_s = reinterpret_cast<int*>(smem + L.off_occ);  // [cands][R]
 
   __shared__ long long s_q, s_base, s_cnt;
-  __shared__ int s_mask, s_nload, s_nal, s_bulk;
+  __shared__ int s_mask, s_nload, s_nal;
 
   const int b = blockIdx.x;
   const int t = threadIdx.x;
   const int lane = lane_id(), warp = warp_id();
+  const unsigned lt_mask = (1u << lane) - 1u;
   int32_t* row = a.in.token_ids + static_cast<long long>(b) * p.row_stride;
+  const int T = a.in.sampled_cols;
+  const int32_t* srow =
+      a.in.sampled ? a.in.sampled + static_cast<long long>(b) * T : nullptr;
 
-  // ---- 1. row bookkeeping + bulk load -----------------------------------
-  if (t == 0) {
+  VoteScratch vs;
+  vs.act = reinterpret_cast<int*>(smem + L.off_warp + warp * L.warp_bytes);
+  vs.hkey = vs.act + (R > 64 ? R : 64);
+  vs.hcnt = vs.hkey + L.H;
+  vs.hmask = L.H - 1;
+  vs.hshift = 33 - __ffs(L.H);
+
+  // ---- 1. row bookkeeping (warp 0) + bulk load ----------------------------
+  int my_samp = -1;  // warp 0, lane j < T: sampled[b, j]
+  if (warp == 0) {
     const long long base = a.in.num_tokens[b];
     long long cnt = 0, q = base;
     int m;
-    if (a.in.sampled) {
+    if (srow) {
+      if (lane < T) my_samp = srow[lane];
       if (a.in.valid_count) {
         cnt = a.in.valid_count[b];
       } else {
-        for (int j = 0; j < a.in.sampled_cols; ++j)
-          cnt += a.in.sampled[static_cast<long long>(b) * a.in.sampled_cols + j] != -1;
+        cnt = __popc(__ballot_sync(SG_FULL_MASK, lane < T && my_samp != -1));
+        for (int j0 = 32; j0 < T; j0 += 32)  // T > 32 (rare)
+          cnt += __popc(__ballot_sync(
+              SG_FULL_MASK, j0 + lane < T && srow[j0 + lane] != -1));
       }
       q = base + cnt;
       m = (cnt > 0) && (q < a.in.limit);
-      a.out.new_counts[b] = static_cast<int32_t>(q);
     } else {
       m = a.in.mask ? (a.in.mask[b] != 0) : 1;
     }
-    const long long nl = q < 0 ? 0 : (q < S ? q : S);
-    const int nload = m ? static_cast<int>(nl) : 0;
-    int nal = nload & ~3;
-    const bool aligned = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
-    if (!aligned) nal = 0;
-    s_q = q; s_base = base; s_cnt = cnt; s_mask = m;
-    s_nload = nload; s_nal = nal; s_bulk = nal > 0;
-    if (nal > 0) {
-      mbar_init(bar, 1);
-      const uint32_t bytes = static_cast<uint32_t>(nal) * 4u;
-      mbar_arrive_expect_tx(bar, bytes);
-      constexpr uint32_t kChunk = 32768;
-      for (uint32_t off = 0; off < bytes; off += kChunk) {
-        const uint32_t n = bytes - off < kChunk ? bytes - off : kChunk;
-        bulk_g2s(reinterpret_cast<unsigned char*>(tok_s) + off,
-                 reinterpret_cast<const unsigned char*>(row) + off, n, bar);
+    if (lane == 0) {
+      if (srow) a.out.new_counts[b] = static_cast<int32_t>(q);
+      const long long nl = q < 0 ? 0 : (q < S ? q : S);
+      const int nload = m ? static_cast<int>(nl) : 0;
+      int nal = nload & ~3;
+      if ((reinterpret_cast<uintptr_t>(row) & 15) != 0) nal = 0;
+      s_q = q; s_base = base; s_cnt = cnt; s_mask = m;
+      s_nload = nload; s_nal = nal;
+      if (nal > 0) {
+        mbar_init(bar, 1);
+        const uint32_t bytes = static_cast<uint32_t>(nal) * 4u;
+        mbar_arrive_expect_tx(bar, bytes);
+        constexpr uint32_t kChunk = 32768;
+        for (uint32_t off = 0; off < bytes; off += kChunk) {
+          const uint32_t n = bytes - off < kChunk ? bytes - off : kChunk;
+          bulk_g2s(reinterpret_cast<unsigned char*>(tok_s) + off,
+                   reinterpret_cast<const unsigned char*>(row) + off, n, bar);
+        }
       }
     }
+  } else {
+    // other warps: empty their vote tables while the loads are in flight
+    vote_table_clear(vs);
+    for (int i = t - 32; i < P + 2; i += kLocalThreads - 32) hist[i] = 0;
   }
   __syncthreads();
   const long long q = s_q;
+  // q clamped into int range: positions are < S < 2^23
+  const int q32 = q > INT32_MAX ? INT32_MAX : (q < INT32_MIN ? INT32_MIN : static_cast<int>(q));
   const int mask = s_mask, nload = s_nload, nal = s_nal;
   // ragged tail (or the whole row when it is not 16-byte aligned)
   for (int i = nal + t; i < nload; i += kLocalThreads) tok_s[i] = row[i];
   bool timed_out = false;
-  if (s_bulk && !mbar_wait(bar, 0)) {
+  if (nal > 0 && !mbar_wait(bar, 0)) {
     // A bulk copy of resident memory always lands; should the bound ever
     // run out, wait once more for the copy in flight, then report the row
     // as failed (num_valid = -1) instead of drafting from partial data.
@@ -164,20 +227,34 @@ __global__ void __launch_bounds__(kLocalThreads)
     if (t == 0) a.out.num_valid[b] = -1;
     return;
   }
-  // scatter-append the sampled ids (update_state, proposer.py:166-188);
-  // the loads above have all landed, so the HBM writes cannot race them
-  if (a.in.sampled) {
-    for (int j = t; j < a.in.sampled_cols; j += kLocalThreads) {
-      const long long pos = s_base + j;
-      const int val = a.in.sampled[static_cast<long long>(b) * a.in.sampled_cols + j];
-      if (j < s_cnt && val != -1 && pos < S && pos >= 0) {
-        row[pos] = val;
-        if (pos < nload) tok_s[pos] = val;
+  if (warp == 0) {
+    if (lane == 0 && nal > 0) mbar_inval(bar);
+    // scatter-append the sampled ids (update_state, proposer.py:166-188);
+    // all loads have landed, so the HBM writes cannot race them
+    if (srow) {
+      const long long base = s_base, cnt = s_cnt;
+      for (int j = lane; j < T; j += 32) {
+        const int val = j < 32 ? my_samp : srow[j];
+        const long long pos = base + j;
+        if (j < cnt && val != -1 && pos < S && pos >= 0) {
+          row[pos] = val;
+          if (pos < nload) tok_s[pos] = val;
+        }
       }
     }
+    __syncwarp();  // this warp's scatter into tok_s is visible below
+    if (mask) {
+      // pattern, newest-first: pat[t] = tok[q-1-t] or -2 before the start
+      // (local_matcher.py:103-112); reads clamp to the buffer like gather
+      for (int i = lane; i < P; i += 32) {
+        const long long x = q - 1 - i;
+        pat[i] = x < 0 ? -2 : tok_s[x < S ? x : S - 1];
+      }
+    }
+    __syncwarp();
+    vote_table_clear(vs);
   }
   __syncthreads();
-  if (t == 0 && s_bulk) mbar_inval(bar);
 
   if (!mask) {
     for (int d = t; d < K; d += kLocalThreads)
@@ -192,209 +269,264 @@ __global__ void __launch_bounds__(kLocalThreads)
     return;
   }
 
-  // ---- 2. pattern + match_back + histogram -------------------------------
-  for (int i = t; i < P; i += kLocalThreads) {
-    const long long x = q - 1 - i;
-    pat[i] = x < 0 ? -2 : tok_s[x < S ? x : S - 1];
-  }
-  for (int i = t; i < P + 2; i += kLocalThreads) hist[i] = 0;
-  __syncthreads();
-
-  const int nw = (nload + 3) >> 2;
-  const int pat0 = pat[0];
-  for (int w = t; w < nw; w += kLocalThreads) {
-    const int i0 = 4 * w;
-    const int4 t4 = reinterpret_cast<const int4*>(tok_s)[w];
-    const int prev = i0 > 0 ? tok_s[i0 - 1] : -1;
-    const int before[4] = {prev, t4.x, t4.y, t4.z};
-    uint32_t packed = 0;
+  // ---- 2. match_back: ordered hit lists per warp segment -----------------
+  const int nw = (nload + 3) >> 2;  // 4-token words
+  const int seg = ((nw + kLocalWarps - 1) / kLocalWarps + 31) & ~31;
+  int* my_hits;
+  int nh = 0;
+  {
+    const int w_begin = warp * seg;
+    const int w_end = min(w_begin + seg, nw);
+    my_hits = hits + static_cast<size_t>(w_begin) * 4;  // 4*seg slots
+    const int4* tok4 = reinterpret_cast<const int4*>(tok_s);
+    const int pt0 = pat[0];
+    // 2a. positions i with tok[i-1] == pat[0], in order
+    int carry = (w_begin > 0 && w_begin < nw) ? tok_s[4 * w_begin - 1] : -1;
+    for (int w0 = w_begin; w0 < w_end; w0 += 32) {
+      const int w = w0 + lane;
+      const int4 cur = w < w_end ? tok4[w] : make_int4(0, 0, 0, 0);
+      int before0 = __shfl_up_sync(SG_FULL_MASK, cur.w, 1);
+      if (lane == 0) before0 = carry;
+      carry = __shfl_sync(SG_FULL_MASK, cur.w, 31);
+      unsigned hm = 0;
+      if (w < w_end) {
+        const int rem = nload - 4 * w;
+        const unsigned vm = rem >= 4 ? 0xFu : ((1u << rem) - 1u);
+        hm = ((before0 == pt0) | ((cur.x == pt0) << 1) |
+              ((cur.y == pt0) << 2) | ((cur.z == pt0) << 3)) & vm;
+      }
+      if (__ballot_sync(SG_FULL_MASK, hm != 0) == 0) continue;
+      const int nz = __popc(hm);
+      const unsigned b0 = __ballot_sync(SG_FULL_MASK, nz & 1);
+      const unsigned b1 = __ballot_sync(SG_FULL_MASK, nz & 2);
+      const unsigned b2 = __ballot_sync(SG_FULL_MASK, nz & 4);
+      int pos = nh + __popc(b0 & lt_mask) + 2 * __popc(b1 & lt_mask) +
+                4 * __popc(b2 & lt_mask);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int i = i0 + k;
-      int m = 0;
-      if (i < nload && before[k] == pat0) {
-        m = 1;
-        for (int tt = 1; tt < P; ++tt) {
-          const int y = i - 1 - tt;
-          const int v = y >= 0 ? tok_s[y] : -1;
-          if (v != pat[tt]) break;
-          ++m;
-        }
-        atomicAdd(&hist[m], 1);
-      }
-      packed |= static_cast<uint32_t>(m) << (8 * k);
-    }
-    reinterpret_cast<uint32_t*>(mb_s)[w] = packed;
-  }
-  __syncthreads();
-
-  // ---- 3. candidates: t-th largest mb for t = 2^c ------------------------
-  if (warp == 0) {
-    if (lane == 0) {
-      int acc = 0;
-      for (int l = P; l >= 1; --l) {
-        acc += hist[l];
-        hist[l] = acc;  // #{mb >= l}
-      }
+      for (int k = 0; k < 4; ++k)
+        if (hm & (1u << k)) my_hits[pos++] = 4 * w + k;
+      nh += __popc(b0) + 2 * __popc(b1) + 4 * __popc(b2);
     }
     __syncwarp();
-    int cand = 0;
-    if (lane < C) {
-      const long long thr = 1ll << lane;
-      for (int l = P; l >= 1; --l) {
-        if (hist[l] >= thr) {
-          cand = l;
-          break;
-        }
-      }
-      const int mml = p.min_match_len > 1 ? p.min_match_len : 1;
-      if (cand < mml) cand = 0;
-    }
-    const int prev = __shfl_up_sync(SG_FULL_MASK, cand, 1);
-    if (lane < C) cand_s[lane] = (lane > 0 && prev == cand) ? 0 : cand;
-  }
-  __syncthreads();
-
-  // ---- 4. earliest R occurrences of every candidate ----------------------
-  {
-    int cr[kMaxCand];
-#pragma unroll
-    for (int c = 0; c < kMaxCand; ++c) cr[c] = c < C ? cand_s[c] : 0;
-    const int wpt = (nw + kLocalThreads - 1) / kLocalThreads;
-    const int w0 = t * wpt;
-    const int w1 = min(w0 + wpt, nw);
-    int hits[kMaxCand];
-#pragma unroll
-    for (int c = 0; c < kMaxCand; ++c) hits[c] = 0;
-    for (int w = w0; w < w1; ++w) {
-      const uint32_t word = reinterpret_cast<const uint32_t*>(mb_s)[w];
-      if (!word) continue;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int m = (word >> (8 * k)) & 0xff;
-        if (!m) continue;
-#pragma unroll
-        for (int c = 0; c < kMaxCand; ++c) hits[c] += (cr[c] > 0 && m >= cr[c]);
-      }
-    }
-    // block exclusive scan of hits[c] in thread order
-    int excl[kMaxCand];
-#pragma unroll
-    for (int c = 0; c < kMaxCand; ++c) {
-      if (c >= C) { excl[c] = 0; continue; }
-      const int inc = warp_incl_scan(hits[c]);
-      if (lane == 31) scan_s[warp * kMaxCand + c] = inc;
-      excl[c] = inc - hits[c];
-    }
-    __syncthreads();
-#pragma unroll
-    for (int c = 0; c < kMaxCand; ++c) {
-      if (c >= C) continue;
-      int off = 0, tot = 0;
-      for (int w = 0; w < kLocalWarps; ++w) {
-        const int v = scan_s[w * kMaxCand + c];
-        if (w < warp) off += v;
-        tot += v;
-      }
-      excl[c] += off;
-      if (t == 0) cnt_s[c] = tot < R ? tot : R;
-    }
-    bool any = false;
-#pragma unroll
-    for (int c = 0; c < kMaxCand; ++c) any |= (cr[c] > 0 && hits[c] > 0 && excl[c] < R);
-    if (any) {
-      for (int w = w0; w < w1; ++w) {
-        const uint32_t word = reinterpret_cast<const uint32_t*>(mb_s)[w];
-        if (!word) continue;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int m = (word >> (8 * k)) & 0xff;
-          if (!m) continue;
-#pragma unroll
-          for (int c = 0; c < kMaxCand; ++c) {
-            if (cr[c] > 0 && m >= cr[c]) {
-              if (excl[c] < R) occ_s[c * R + excl[c]] = 4 * w + k;
-              ++excl[c];
+    // 2b. extend every hit; consecutive lanes take consecutive hits
+    const int pt1 = P > 1 ? pat[1] : INT32_MIN;
+    const int pt2 = P > 2 ? pat[2] : INT32_MIN;
+    const int pt3 = P > 3 ? pat[3] : INT32_MIN;
+    int h1 = 0, h2 = 0, h3 = 0, h4 = 0, mmax = 0;
+    for (int i = lane; i < nh; i += 32) {
+      const int e = my_hits[i];
+      const int t1 = e >= 2 ? tok_s[e - 2] : -1;
+      const int t2 = e >= 3 ? tok_s[e - 3] : -1;
+      const int t3 = e >= 4 ? tok_s[e - 4] : -1;
+      int m = 1;
+      if (t1 == pt1) {
+        m = 2;
+        if (t2 == pt2) {
+          m = 3;
+          if (t3 == pt3) {
+            m = 4;
+            for (int tt = 4; tt < P; ++tt) {
+              const int y = e - 1 - tt;
+              const int v = y >= 0 ? tok_s[y] : -1;
+              if (v != pat[tt]) break;
+              ++m;
             }
           }
         }
       }
+      if (m > P) m = P;
+      h1 += m == 1;
+      h2 += m == 2;
+      h3 += m == 3;
+      h4 += m == 4;
+      if (m > 4) atomicAdd(&hist[m], 1);
+      mmax = max(mmax, m);
+      my_hits[i] = (e << 8) | m;
+    }
+    h1 = warp_sum(h1);
+    h2 = warp_sum(h2);
+    h3 = warp_sum(h3);
+    h4 = warp_sum(h4);
+    mmax = __reduce_max_sync(SG_FULL_MASK, mmax);
+    if (lane == 0) {
+      wlen[warp] = nh;
+      wmax[warp] = mmax;
+      if (h1) atomicAdd(&hist[1], h1);
+      if (h2) atomicAdd(&hist[2], h2);
+      if (h3) atomicAdd(&hist[3], h3);
+      if (h4) atomicAdd(&hist[4], h4);
     }
   }
   __syncthreads();
 
-  // ---- 5. one warp per candidate: vote + score ---------------------------
-  {
-    unsigned char* wbase = smem + L.off_warp + warp * L.warp_bytes;
-    VoteScratch vs;
-    vs.act = reinterpret_cast<int*>(wbase);
-    vs.hkey = vs.act + R;
-    vs.hcnt = vs.hkey + L.H;
-    vs.hmask = L.H - 1;
-    for (int c = warp; c < C; c += kLocalWarps) {
-      const int cand = cand_s[c];
-      int* chain = chain_s + c * K;
-      if (cand == 0) {
-        for (int d = lane; d < K; d += 32) chain[d] = -1;
-        if (lane == 0) {
-          score_s[c] = 0.0f;
-          emit_s[c] = 0;
+  // ---- 3. candidates and their earliest R occurrences -------------------
+  const int cand_lane = warp_candidates(hist, P, C, p.min_match_len);
+  if (warp == 0 && lane < C) cand_s[lane] = cand_lane;
+  int total_hits = 0;
+#pragma unroll
+  for (int w = 0; w < kLocalWarps; ++w) total_hits += wlen[w];
+  // Few hits: each candidate's warp walks every list itself (no extra
+  // barriers). Many hits: every warp counts its own list per candidate,
+  // then writes its share at the prefix offset.
+  const bool walk = total_hits <= kWalkHits;
+  if (!walk) {
+    const int my_max = wmax[warp];
+    int mycnt = 0;  // lane c: hits in this warp's list with mb >= cand_c
+    {
+      int cr[NC], k[NC];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        cr[c] = c < C ? __shfl_sync(SG_FULL_MASK, cand_lane, c) : 0;
+        if (cr[c] > my_max) cr[c] = 0;  // no entry of this list qualifies
+        k[c] = 0;
+      }
+      for (int i = lane; i < nh; i += 32) {
+        const int m = my_hits[i] & 0xff;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) k[c] += (cr[c] > 0 && m >= cr[c]);
+      }
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        if (c < C) {
+          const int tot = __reduce_add_sync(SG_FULL_MASK, k[c]);
+          if (lane == c) mycnt = tot;
         }
-        continue;
       }
-      const int* occ = occ_s + c * R;
-      auto cont = [&](int r, int d) -> int {
-        const long long x = static_cast<long long>(occ[r]) + d;
-        return x < q ? tok_s[x < S ? x : S - 1] : -1;
-      };
-      const ExpandResult er = warp_expand<RJ>(
-          cont, cnt_s[c], K, spec_cap(p, cand), p.min_token_prob,
-          p.vote_alpha, vs, chain);
+    }
+    if (lane < C) wcnt[warp * kMaxCand + lane] = mycnt;
+    __syncthreads();
+    // earliest R end positions per candidate, written at this warp's
+    // offset (local_matcher.py:160-184)
+    for (int c = 0; c < C; ++c) {
+      const int cand = __shfl_sync(SG_FULL_MASK, cand_lane, c);
+      const int k = __shfl_sync(SG_FULL_MASK, mycnt, c);
+      if (cand == 0 || k == 0) continue;
+      int off = 0;
+      for (int w = 0; w < warp; ++w) off += wcnt[w * kMaxCand + c];
+      if (off >= R) continue;
+      int* oc = occ_s + c * R;
+      for (int i0 = 0; i0 < nh && off < R; i0 += 32) {
+        const int i = i0 + lane;
+        const int e = i < nh ? my_hits[i] : 0;
+        const bool hit = i < nh && (e & 0xff) >= cand;
+        const unsigned bal = __ballot_sync(SG_FULL_MASK, hit);
+        const int r = off + __popc(bal & lt_mask);
+        if (hit && r < R) oc[r] = e >> 8;
+        off += __popc(bal);
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---- 3b. one warp per candidate: vote + score --------------------------
+  for (int c = warp; c < C; c += kLocalWarps) {
+    const int cand = __shfl_sync(SG_FULL_MASK, cand_lane, c);
+    int* chain = chain_s + c * K;
+    if (cand == 0) {
+      for (int d = lane; d < K; d += 32) chain[d] = -1;
       if (lane == 0) {
-        score_s[c] = er.score;
-        emit_s[c] = er.emit;
+        score_s[c] = 0.0f;
+        emit_s[c] = 0;
       }
+      continue;
+    }
+    const int* oc = occ_s + c * R;
+    int n = 0;
+    if (walk) {
+      // earliest R end positions with mb >= cand, in position order
+      int* ocw = occ_s + c * R;
+      for (int w = 0; w < kLocalWarps && n < R; ++w) {
+        if (wmax[w] < cand) continue;
+        const int* lst = hits + static_cast<size_t>(w) * seg * 4;
+        const int len = wlen[w];
+        for (int i0 = 0; i0 < len && n < R; i0 += 32) {
+          const int e = i0 + lane < len ? lst[i0 + lane] : 0;
+          const bool hit = (e & 0xff) >= cand;
+          const unsigned bal = __ballot_sync(SG_FULL_MASK, hit);
+          const int r = n + __popc(bal & lt_mask);
+          if (hit && r < R) ocw[r] = e >> 8;
+          n += __popc(bal);
+        }
+      }
+      __syncwarp();
+    } else {
+      for (int w = 0; w < kLocalWarps; ++w) n += wcnt[w * kMaxCand + c];
+    }
+    if (n > R) n = R;
+    // continuation tokens (local_matcher.py:186-195): tok[e + d] if e+d < q
+    auto key_of = [&](int i) -> int { return oc[i]; };
+    auto cont = [&](int e, int d) -> int {
+      const int x = e + d;  // e < S < 2^23, d < 64
+      return x < q32 ? tok_s[x < S ? x : S - 1] : -1;
+    };
+    const ExpandResult er = warp_expand<RJ>(
+        key_of, cont, n, K, spec_cap(p, cand), /*stop_at_cap=*/true,
+        p.min_token_prob, p.vote_alpha, vs, chain);
+    if (lane == 0) {
+      score_s[c] = er.score;
+      emit_s[c] = er.emit;
     }
   }
   __syncthreads();
 
-  // ---- 6. select_local_best (local_matcher.py:245-263) -------------------
-  __shared__ int s_best;
-  if (t == 0) {
-    int best = 0;
-    float bv = __fadd_rn(score_s[0], __fmul_rn(static_cast<float>(cand_s[0]), 1e-6f));
-    for (int c = 1; c < C; ++c) {
-      const float v = __fadd_rn(score_s[c], __fmul_rn(static_cast<float>(cand_s[c]), 1e-6f));
-      if (v > bv) {
-        bv = v;
-        best = c;
-      }
-    }
+  // ---- 4. select_local_best (local_matcher.py:245-263) -------------------
+  if (warp == 0) {
+    // value = score + f32(cand) * 1e-6; the first maximum wins. Floats map
+    // to unsigned keys with the same order (-0 folded into +0).
+    float v = -INFINITY;
+    if (lane < C)
+      v = __fadd_rn(__fadd_rn(score_s[lane],
+                              __fmul_rn(static_cast<float>(cand_s[lane]), 1e-6f)),
+                    0.0f);
+    const uint32_t bits = __float_as_uint(v);
+    const uint32_t key = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
+    const uint32_t kmax = __reduce_max_sync(SG_FULL_MASK, key);
+    const int idx = __reduce_min_sync(SG_FULL_MASK, key == kmax ? lane : 32);
+    const uint32_t kb = (kmax & 0x80000000u) ? (kmax & 0x7fffffffu) : ~kmax;
+    const float bvf = __uint_as_float(kb);
+    int best = idx;
+    const float bv = bvf;
     // Candidates c >= n_cand have thresholds above S, hence value 0.0; the
     // first of them is the argmax only when every value above is negative
     // (possible with a negative min_token_prob and alpha).
     if (C < p.num_backoff && 0.0f > bv) best = -1;
-    s_best = best;
-    a.out.num_valid[b] = best >= 0 ? emit_s[best] : 0;
-    if (a.out.best_score) a.out.best_score[b] = best >= 0 ? score_s[best] : 0.0f;
-    if (a.out.best_len) a.out.best_len[b] = best >= 0 ? cand_s[best] : 0;
-    if (a.out.best_occ) a.out.best_occ[b] = best >= 0 ? cnt_s[best] : 0;
-    if (a.out.row_mask) a.out.row_mask[b] = 1;
+    const int emit = best >= 0 ? emit_s[best] : 0;
+    for (int d = lane; d < K; d += 32)
+      a.out.draft[static_cast<long long>(b) * K + d] =
+          d < emit ? chain_s[best * K + d] : -1;
+    if (lane == 0) {
+      a.out.num_valid[b] = emit;
+      if (a.out.best_score)
+        a.out.best_score[b] = best >= 0 ? score_s[best] : 0.0f;
+      if (a.out.best_len) a.out.best_len[b] = best >= 0 ? cand_s[best] : 0;
+      if (a.out.best_occ) {
+        // occurrence count of the chosen candidate: min(#{mb >= cand}, R)
+        int occ = 0;
+        if (best >= 0 && cand_s[best] > 0) {
+          int ge = 0;
+          for (int l = cand_s[best]; l <= P; ++l) ge += hist[l];
+          occ = ge < R ? ge : R;
+        }
+        a.out.best_occ[b] = occ;
+      }
+      if (a.out.row_mask) a.out.row_mask[b] = 1;
+    }
   }
-  __syncthreads();
-  const int best = s_best;
-  const int emit = best >= 0 ? emit_s[best] : 0;
-  for (int d = t; d < K; d += kLocalThreads)
-    a.out.draft[static_cast<long long>(b) * K + d] = d < emit ? chain_s[best * K + d] : -1;
+}
+
+template <int RJ, int NC>
+static int launch_local_nc(const LocalArgs& a, size_t smem, cudaStream_t st) {
+  static int cache[64] = {0};
+  const int rc = ensure_dyn_smem(local_draft_kernel<RJ, NC>, smem, cache);
+  if (rc != SG_OK) return rc;
+  local_draft_kernel<RJ, NC><<<a.p.batch, kLocalThreads, smem, st>>>(a);
+  return check_launch();
 }
 
 template <int RJ>
 static int launch_local(const LocalArgs& a, size_t smem, cudaStream_t st) {
-  static int cache[64] = {0};
-  const int rc = ensure_dyn_smem(local_draft_kernel<RJ>, smem, cache);
-  if (rc != SG_OK) return rc;
-  local_draft_kernel<RJ><<<a.p.batch, kLocalThreads, smem, st>>>(a);
-  return check_launch();
+  return a.n_cand <= 8 ? launch_local_nc<RJ, 8>(a, smem, st)
+                       : launch_local_nc<RJ, kMaxCand>(a, smem, st);
 }
 
 }  // namespace sg
@@ -411,6 +543,7 @@ extern "C" int sg_local_draft(const sg_draft_params* params,
       p.k > 64 || p.max_pattern_len < 1 || p.max_pattern_len > 255 ||
       p.max_occurrences < 1 || p.max_occurrences > 1024 || p.num_backoff < 1)
     return SG_ERR_INVALID;
+  if (p.seq_len >= (1 << 23)) return SG_ERR_UNSUPPORTED;
   if (p.batch == 0) return SG_OK;
   if (!in->num_tokens || !in->token_ids || !out->draft || !out->num_valid)
     return SG_ERR_INVALID;

@@ -140,24 +140,30 @@ __global__ void __launch_bounds__(kExWarps * 32)
   extern __shared__ __align__(16) unsigned char smem[];
   const int warp = warp_id();
   const int row = blockIdx.x * kExWarps + warp;
-  unsigned char* wb = smem + static_cast<size_t>(warp) * (4 * R + 8 * H);
+  const int RA = R > 64 ? R : 64;
+  unsigned char* wb = smem + static_cast<size_t>(warp) * (4 * RA + 8 * H);
   VoteScratch vs;
   vs.act = reinterpret_cast<int*>(wb);
-  vs.hkey = vs.act + R;
+  vs.hkey = vs.act + RA;
   vs.hcnt = vs.hkey + H;
   vs.hmask = H - 1;
+  vs.hshift = 33 - __ffs(H);
   if (row >= N) return;
   const int32_t* c = cont + static_cast<long long>(row) * R * K;
   long long n_occ = num_occ[row];
   if (n_occ > R) n_occ = R;
   if (n_occ < 0) n_occ = 0;
   const long long cp = cap ? cap[row] : K;
+  vote_table_clear(vs);
+  auto key_of = [](int i) -> int { return i; };
   auto fn = [&](int r, int d) -> int {
     return __ldg(c + static_cast<long long>(r) * K + d);
   };
   int32_t* ch = chain + static_cast<long long>(row) * K;
-  const ExpandResult er = warp_expand<RJ>(fn, static_cast<int>(n_occ), K, cp,
-                                          min_prob, alpha, vs, ch);
+  // the operator returns num_valid too, so every depth is expanded
+  const ExpandResult er = warp_expand<RJ>(
+      key_of, fn, static_cast<int>(n_occ), K, cp, /*stop_at_cap=*/false,
+      min_prob, alpha, vs, ch);
   if (lane_id() == 0) {
     nv_out[row] = er.num_valid;
     emit_out[row] = er.emit;
@@ -229,7 +235,8 @@ static int launch_expand(const int32_t* cont, int N, int R, int K,
                          int64_t* nv, int64_t* emit, float* score,
                          cudaStream_t st) {
   const int H = static_cast<int>(next_pow2_u32(2 * R > 64 ? 2 * R : 64));
-  const size_t smem = static_cast<size_t>(kExWarps) * (4 * R + 8 * H);
+  const size_t smem =
+      static_cast<size_t>(kExWarps) * (4 * (R > 64 ? R : 64) + 8 * H);
   static int cache[64] = {0};
   const int rc = ensure_dyn_smem(expand_kernel<RJ>, smem, cache);
   if (rc != SG_OK) return rc;

@@ -9,13 +9,19 @@
 // valid while the count is positive and the probability >= min_token_prob;
 // the score sums the probabilities of valid depths below the cap.
 //
-// B200 design: one warp per candidate. Instead of sorting the R values of
-// every depth (the Triton kernel) or comparing all pairs (the torch path),
-// the warp keeps a compacted list of the surviving occurrences. Up to 32
-// survivors vote with __match_any_sync; larger sets count into a per-warp
-// open-addressing table in shared memory. After each depth the list is
-// compacted to the occurrences that matched the winner (ballot + popc), so
-// later depths touch only the survivors.
+// B200 design: one warp per candidate, survivors resident in registers.
+// Instead of sorting the R values of every depth (the Triton kernel) or
+// comparing all pairs (the torch path), each lane holds up to RJ
+// occurrences and an alive bit per slot; a depth reads one token per alive
+// slot and votes:
+//   * <= 32 survivors (one per lane): each lane counts its token among the
+//     32 in a shared buffer (8 vector loads), then two warp reductions;
+//   * more: a per-warp open-addressing table in shared memory, one CAS
+//     insert + one atomic add per token, all of a lane's in flight together;
+//     every lane then empties the slots it used.
+// The winner's non-matching occurrences drop their alive bit; once <= 32
+// remain they are compacted to one per lane. While all survivors agree, up
+// to 8 depths are committed at once from a shared lookahead.
 #pragma once
 
 #include "sg_common.cuh"
@@ -23,153 +29,282 @@
 namespace sg {
 
 struct ExpandResult {
-  int num_valid;  // leading valid depths
+  int num_valid;  // leading valid depths (computed ones when stopping at cap)
   int emit;       // min(num_valid, max(cap, 0))
   float score;
 };
 
 // Per-warp shared-memory scratch for the vote.
 struct VoteScratch {
-  int* act;    // [R] surviving occurrence indices
+  int* act;    // [max(R, 64)] compaction / small-vote buffer
   int* hkey;   // [H] hash keys (-1 = empty; -1 is never a voting token)
   int* hcnt;   // [H] counts
   int hmask;   // H - 1 (H power of two, >= 2 * R)
+  int hshift;  // 32 - log2(H)
 };
 
-__device__ __forceinline__ uint32_t hash_tok(int v) {
-  uint32_t x = static_cast<uint32_t>(v);
-  x *= 0x9E3779B1u;
-  return x ^ (x >> 15);
+// Empty the table (once per warp; every vote leaves it empty again).
+__device__ __forceinline__ void vote_table_clear(const VoteScratch& vs) {
+  for (int h = lane_id(); h <= vs.hmask; h += 32) {
+    vs.hkey[h] = -1;
+    vs.hcnt[h] = 0;
+  }
+  __syncwarp();
 }
 
-// Order key: larger for (higher count, then smaller token).
+// Warp max of counts, then the min token among lanes holding that count.
+// (__match_any_sync is avoided throughout: it costs ~380 cycles on sm_100a
+// against ~30 for a reduction or a shared-memory load.)
 __device__ __forceinline__ void vote_best(int cnt, int tok, int& best_cnt,
                                           int& best_tok) {
-  // warp max of counts, then min token among the lanes holding that count
   const int cmax = __reduce_max_sync(SG_FULL_MASK, cnt);
   const int cand = (cnt == cmax && cnt > 0) ? tok : INT32_MAX;
   // __reduce_min_sync on signed ints orders tokens the way torch's min does
-  const int tmin = __reduce_min_sync(SG_FULL_MASK, cand);
+  best_tok = __reduce_min_sync(SG_FULL_MASK, cand);
   best_cnt = cmax;
-  best_tok = tmin;
+}
+
+// Plurality vote over one token per lane (-1 = no vote): every lane counts
+// its token among the 32 in a shared buffer. Also returns n_act, the number
+// of voting lanes.
+__device__ __forceinline__ void vote_small(int v, int* buf, int& best_cnt,
+                                           int& best_tok, int& n_act) {
+  const int lane = lane_id();
+  buf[lane] = v;
+  __syncwarp();
+  const int4* b4 = reinterpret_cast<const int4*>(buf);
+  int c = 0, na = 0;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const int4 w = b4[q];
+    c += (w.x == v) + (w.y == v) + (w.z == v) + (w.w == v);
+    na += (w.x != -1) + (w.y != -1) + (w.z != -1) + (w.w != -1);
+  }
+  __syncwarp();
+  vote_best(v != -1 ? c : 0, v, best_cnt, best_tok);
+  n_act = na;
+}
+
+// Plurality vote over RJ slots per lane (-1 = no vote) with the hash table:
+// every token is inserted on its own (all of a lane's inserts in flight
+// together) and counted with one shared-memory atomic.
+template <int RJ>
+__device__ __forceinline__ void vote_hash(const int (&v)[RJ], int nslots,
+                                          const VoteScratch& vs,
+                                          int& best_cnt, int& best_tok,
+                                          int& n_act) {
+  int hh[RJ], got[RJ];
+  unsigned pend = 0;
+  int mine = 0;
+#pragma unroll
+  for (int j = 0; j < RJ; ++j) {
+    got[j] = -1;
+    hh[j] = 0;
+    if (j < nslots && v[j] != -1) {
+      pend |= 1u << j;
+      ++mine;
+      hh[j] = static_cast<int>((static_cast<uint32_t>(v[j]) * 0x9E3779B1u) >>
+                               vs.hshift);
+    }
+  }
+  for (int probe = 0; pend && probe <= vs.hmask; ++probe) {
+    int old[RJ];
+#pragma unroll
+    for (int j = 0; j < RJ; ++j)
+      if (pend & (1u << j)) old[j] = atomicCAS(&vs.hkey[hh[j]], -1, v[j]);
+#pragma unroll
+    for (int j = 0; j < RJ; ++j) {
+      if (pend & (1u << j)) {
+        if (old[j] == -1 || old[j] == v[j]) {
+          got[j] = hh[j];
+          pend &= ~(1u << j);
+        } else {
+          hh[j] = (hh[j] + 1) & vs.hmask;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < RJ; ++j)
+    if (got[j] >= 0) atomicAdd(&vs.hcnt[got[j]], 1);
+  __syncwarp();
+  int my_cnt = 0, my_tok = INT32_MAX;
+#pragma unroll
+  for (int j = 0; j < RJ; ++j) {
+    if (got[j] >= 0) {
+      const int c = vs.hcnt[got[j]];
+      if (c > my_cnt || (c == my_cnt && v[j] < my_tok)) {
+        my_cnt = c;
+        my_tok = v[j];
+      }
+    }
+  }
+  n_act = __reduce_add_sync(SG_FULL_MASK, mine);
+  vote_best(my_cnt, my_tok, best_cnt, best_tok);
+  // empty the used slots (duplicates are harmless)
+#pragma unroll
+  for (int j = 0; j < RJ; ++j) {
+    if (got[j] >= 0) {
+      vs.hkey[got[j]] = -1;
+      vs.hcnt[got[j]] = 0;
+    }
+  }
+  __syncwarp();
 }
 
 // Expand one candidate with the calling (full) warp.
-//   cont(r, d): continuation token of occurrence r at depth d (-1 = none)
-//   n_occ: occurrences (rows r < n_occ are active at depth 0)
-//   chain_out: K ints written by lane 0..K-1 (warp-strided)
+//   key_of(i): key of the i-th occurrence, i < n_occ (read once)
+//   cont(key, d): continuation token of that occurrence at depth d (-1 =
+//                 none)
+//   stop_at_cap: stop expanding at depth cap. Depths >= cap change neither
+//                num_emit nor the score nor chain[:num_emit], so the
+//                drafter (which only uses those) sets it; the expand_chain
+//                operator, which also returns num_valid, does not.
+//   chain_out: K ints; entries past the last computed depth are -1.
 // RJ: max occurrences per lane (R <= 32 * RJ).
-template <int RJ, class ContFn>
-__device__ ExpandResult warp_expand(ContFn cont, int n_occ, int K,
-                                    long long cap, float min_prob,
-                                    float alpha, const VoteScratch& vs,
-                                    int* chain_out) {
+template <int RJ, class KeyFn, class ContFn>
+__device__ ExpandResult warp_expand(KeyFn key_of, ContFn cont, int n_occ,
+                                    int K, long long cap, bool stop_at_cap,
+                                    float min_prob, float alpha,
+                                    const VoteScratch& vs, int* chain_out) {
   const int lane = lane_id();
-  int n = n_occ;
-  for (int i = lane; i < n; i += 32) vs.act[i] = i;
-  __syncwarp();
+  const unsigned lt_mask = (1u << lane) - 1u;
+  int depth_end = K;
+  if (stop_at_cap)
+    depth_end = cap < K ? static_cast<int>(cap > 0 ? cap : 0) : K;
+
+  int e[RJ];
+  unsigned amask = 0;  // alive slots of this lane
+#pragma unroll
+  for (int j = 0; j < RJ; ++j) {
+    const int i = j * 32 + lane;
+    e[j] = 0;
+    if (i < n_occ) {
+      e[j] = key_of(i);
+      amask |= 1u << j;
+    }
+  }
+  int n = n_occ;               // survivors (warp-uniform)
+  int nslots = (n + 31) >> 5;  // slots that may hold survivors
+  const bool unit_alpha = alpha == 0.0f;
+  int* ref = vs.act + 32;      // lookahead tokens of the first survivor
 
   float prob = 1.0f;
   float score = 0.0f;
   int nv = 0;
   int written = 0;  // depths [0, written) of chain_out are final
-  bool alive = n > 0;
-  for (int d = 0; d < K && alive; ++d) {
-    // gather this depth's tokens for the survivors
-    int rr[RJ];
-    int vv[RJ];
-    int n_act = 0;
+  int first = 0;    // lowest alive lane when nslots == 1
+  for (int d = 0; d < depth_end && n > 0; ++d) {
+    if (nslots == 1) {
+      // Unanimous lookahead: while every survivor has the same token, the
+      // vote is that token with count = active = survivors, so the depths
+      // can be committed without voting (same fp32 steps).
+      const bool alive = amask & 1u;
+      const int ahead = min(8, depth_end - d);
+      int tk[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        tk[u] = (u < ahead && alive) ? cont(e[0], d + u) : -1;
+      if (lane == first) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) ref[u] = tk[u];
+      }
+      __syncwarp();
+      int agree = ahead;
+#pragma unroll
+      for (int u = 7; u >= 0; --u) {
+        const int r = ref[u];
+        if (u < ahead && (r == -1 || (alive && tk[u] != r))) agree = u;
+      }
+      const int run = __reduce_min_sync(SG_FULL_MASK, agree);
+      if (run > 0) {
+        int tok_u[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) tok_u[u] = ref[u];
+        const float ratio = unit_alpha
+            ? 1.0f
+            : __fdiv_rn(static_cast<float>(n),
+                        __fadd_rn(static_cast<float>(n), alpha));
+        bool stop = false;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (u < run && !stop) {
+            prob = __fmul_rn(prob, ratio);
+            const bool valid = prob >= min_prob;
+            if (lane == 0) chain_out[d + u] = valid ? tok_u[u] : -1;
+            written = d + u + 1;
+            if (!valid) {
+              stop = true;
+            } else {
+              ++nv;
+              if (static_cast<long long>(d + u) < cap)
+                score = __fadd_rn(score, prob);
+            }
+          }
+        }
+        __syncwarp();
+        if (stop) break;
+        d += run - 1;  // the loop's ++d moves to the first undecided depth
+        continue;
+      }
+      __syncwarp();
+    }
+    int v[RJ];
 #pragma unroll
     for (int j = 0; j < RJ; ++j) {
-      const int i = j * 32 + lane;
-      rr[j] = -1;
-      vv[j] = -1;
-      if (i < n) {
-        rr[j] = vs.act[i];
-        vv[j] = cont(rr[j], d);
-      }
-      n_act += __popc(__ballot_sync(SG_FULL_MASK, vv[j] != -1));
-      if (j * 32 + 32 >= n) break;
+      v[j] = -1;
+      if (j < nslots && (amask & (1u << j))) v[j] = cont(e[j], d);
     }
-    int best_cnt = 0, best_tok = -1;
-    if (n_act > 0) {
-      if (n <= 32) {
-        const int v = vv[0];
-        const unsigned act_mask = __ballot_sync(SG_FULL_MASK, v != -1);
-        const unsigned peers = __match_any_sync(SG_FULL_MASK, v);
-        const int c = (v != -1) ? __popc(peers & act_mask) : 0;
-        vote_best(c, v, best_cnt, best_tok);
-      } else {
-        // clear the table
-        for (int h = lane; h <= vs.hmask; h += 32) {
-          vs.hkey[h] = -1;
-          vs.hcnt[h] = 0;
-        }
-        __syncwarp();
-        int slot[RJ];
-#pragma unroll
-        for (int j = 0; j < RJ; ++j) {
-          slot[j] = -1;
-          const int v = vv[j];
-          if (v != -1) {
-            uint32_t h = hash_tok(v) & vs.hmask;
-            for (int probe = 0; probe <= vs.hmask; ++probe) {
-              const int old = atomicCAS(&vs.hkey[h], -1, v);
-              if (old == -1 || old == v) {
-                atomicAdd(&vs.hcnt[h], 1);
-                slot[j] = static_cast<int>(h);
-                break;
-              }
-              h = (h + 1) & vs.hmask;
-            }
-          }
-          if (j * 32 + 32 >= n) break;
-        }
-        __syncwarp();
-        int my_cnt = 0, my_tok = INT32_MAX;
-#pragma unroll
-        for (int j = 0; j < RJ; ++j) {
-          if (slot[j] >= 0) {
-            const int c = vs.hcnt[slot[j]];
-            const int v = vv[j];
-            if (c > my_cnt || (c == my_cnt && v < my_tok)) {
-              my_cnt = c;
-              my_tok = v;
-            }
-          }
-          if (j * 32 + 32 >= n) break;
-        }
-        vote_best(my_cnt, my_tok, best_cnt, best_tok);
-        __syncwarp();
-      }
+    int best_cnt = 0, best_tok = -1, n_act = 0;
+    if (nslots == 1) {
+      vote_small(v[0], vs.act, best_cnt, best_tok, n_act);
+    } else {
+      vote_hash<RJ>(v, nslots, vs, best_cnt, best_tok, n_act);
     }
-    // fp32 chain probability, correctly rounded, no contraction
-    const float denom = __fadd_rn(static_cast<float>(n_act > 1 ? n_act : 1),
-                                  alpha);
-    prob = __fmul_rn(prob, __fdiv_rn(static_cast<float>(best_cnt), denom));
+    // fp32 chain probability, correctly rounded, no contraction; a
+    // unanimous vote with alpha 0 divides a count by itself: exactly 1
+    float ratio;
+    if (unit_alpha && best_cnt == n_act && n_act > 0) {
+      ratio = 1.0f;
+    } else {
+      const float denom =
+          __fadd_rn(static_cast<float>(n_act > 1 ? n_act : 1), alpha);
+      ratio = __fdiv_rn(static_cast<float>(best_cnt), denom);
+    }
+    prob = __fmul_rn(prob, ratio);
     const bool valid = best_cnt > 0 && prob >= min_prob;
     if (lane == 0) chain_out[d] = valid ? best_tok : -1;
     written = d + 1;
-    if (!valid) {
-      alive = false;
-      break;
-    }
+    if (!valid) break;
     ++nv;
     if (static_cast<long long>(d) < cap) score = __fadd_rn(score, prob);
-    // keep the occurrences that agree with the winner
-    int base = 0;
+    // keep the occurrences that agree with the winner: exactly best_cnt
 #pragma unroll
-    for (int j = 0; j < RJ; ++j) {
-      const bool keep = (j * 32 + lane < n) && vv[j] == best_tok;
-      const unsigned bal = __ballot_sync(SG_FULL_MASK, keep);
-      if (keep) vs.act[base + __popc(bal & ((1u << lane) - 1u))] = rr[j];
-      base += __popc(bal);
-      if (j * 32 + 32 >= n) break;
+    for (int j = 0; j < RJ; ++j)
+      if (j < nslots && v[j] != best_tok) amask &= ~(1u << j);
+    n = best_cnt;
+    if (nslots > 1 && n <= 32) {
+      // compact the survivors to one per lane
+      int base = 0;
+#pragma unroll
+      for (int j = 0; j < RJ; ++j) {
+        if (j < nslots) {
+          const bool alive = (amask >> j) & 1u;
+          const unsigned bal = __ballot_sync(SG_FULL_MASK, alive);
+          if (alive) vs.act[base + __popc(bal & lt_mask)] = e[j];
+          base += __popc(bal);
+        }
+      }
+      __syncwarp();
+      e[0] = lane < n ? vs.act[lane] : 0;
+      amask = lane < n ? 1u : 0u;
+      nslots = 1;
+      __syncwarp();
     }
-    n = base;
-    __syncwarp();
+    if (nslots == 1)
+      first = __ffs(__ballot_sync(SG_FULL_MASK, amask & 1u)) - 1;
   }
-  // depths past the first invalid one (or all, with no occurrences)
+  // depths past the last computed one
   for (int dd = written + lane; dd < K; dd += 32) chain_out[dd] = -1;
   __syncwarp();
   ExpandResult res;
