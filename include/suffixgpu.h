@@ -150,6 +150,98 @@ int sg_expand_chain(const int32_t* cont, int32_t rows, int32_t max_occ,
                     int64_t* num_valid, int64_t* num_emit, float* score,
                     sg_stream_t stream);
 
+/* ---- suffix array (suffix_gpu/suffix_array.py) -------------------------- */
+
+/* Workspace bytes sg_build_suffix_array needs for n tokens (~36 n). */
+size_t sg_suffix_array_workspace_size(int64_t n);
+
+/* build_suffix_array (suffix_array.py:15-63): sa_out[0..n) = start
+ * positions of the suffixes of tokens[0..n) in lexicographic order (signed
+ * token order, end of string first). Identical to the reference's result
+ * (the suffix array is unique). Prefix doubling over still-tied suffixes
+ * with a device radix sort; the call reads the active count back once per
+ * doubling round, so it synchronises `stream` (run it from its own host
+ * thread / stream for a background rebuild). rounds_out (host pointer,
+ * may be NULL) receives the number of doubling rounds after the initial
+ * token sort. n < 2^31 - 1. */
+int sg_build_suffix_array(const int32_t* tokens, int64_t n, int32_t* sa_out,
+                          void* workspace, size_t workspace_bytes,
+                          int32_t* rounds_out, sg_stream_t stream);
+
+/* ---- suffix-array search (suffix_gpu/sa_search.py) ---------------------- */
+
+/* search_interval (sa_search.py:66-107, triton_kernels.py:284-302): SA
+ * interval [start, end) of suffixes starting with each pattern row
+ * pattern[b, :width] of length pattern_len[b], by the reference's fixed
+ * ceil(log2(n+1))-iteration merged lower/upper bound search. */
+int sg_sa_search(const int32_t* sa, const int32_t* corpus, int64_t n,
+                 const int32_t* pattern, int32_t batch, int32_t width,
+                 const int64_t* pattern_len, int64_t* out_start,
+                 int64_t* out_end, sg_stream_t stream);
+
+/* suffix_match_backoff (sa_search.py:110-163): for every row, searches the
+ * suffixes of length 1..max_len of query[b, :query_len[b]] and, per cap c,
+ * returns the longest found length <= caps[c] with its SA interval (0s when
+ * none). Outputs [B, num_caps] int64. row_mask (may be NULL) skips rows. */
+int sg_suffix_match_backoff(const int32_t* sa, const int32_t* corpus,
+                            int64_t n, const int32_t* query, int32_t batch,
+                            int32_t query_width, const int64_t* query_len,
+                            int32_t max_len, const int64_t* caps,
+                            int32_t num_caps, const uint8_t* row_mask,
+                            int64_t* out_len, int64_t* out_start,
+                            int64_t* out_end, sg_stream_t stream);
+
+/* ---- global index (suffix_gpu/global_index.py) --------------------------- */
+
+/* GlobalIndex._delta_match_backoff (global_index.py:465-546) over the delta
+ * buffer; delta_len is a device int64 scalar. Outputs: out_len [B, C]
+ * (min(longest match, cap)), out_pos [B, C, R] earliest start positions
+ * (zero-padded), out_cnt [B, C] (clamped to R). num_caps <= 16. */
+int sg_delta_match_backoff(const int32_t* delta, int64_t delta_capacity,
+                           const int64_t* delta_len, const int32_t* query,
+                           int32_t batch, int32_t query_width,
+                           const int64_t* query_len, int32_t max_len,
+                           const int64_t* caps, int32_t num_caps,
+                           int32_t max_occ, const uint8_t* row_mask,
+                           int64_t* out_len, int64_t* out_pos,
+                           int64_t* out_cnt, sg_stream_t stream);
+
+/* SuffixGPUDrafter._gather_tails (proposer.py:110-125): last
+ * min(count, P) tokens of each row, oldest first, zero-padded to P. */
+int sg_gather_tails(const int32_t* token_ids, int64_t row_stride,
+                    int32_t seq_len, const int32_t* counts, int32_t batch,
+                    int32_t pattern_len, int32_t* tails, int64_t* tail_len,
+                    sg_stream_t stream);
+
+/* Tail of GlobalIndex._query_backoff (global_index.py:321-370) and
+ * _gather_cont (:443-463): SA-vs-delta choice per cap, adjacent-duplicate
+ * removal, strided SA interval sampling, continuation block cont
+ * [B, C, R, K] int32 (-1 padded), match_len / occ_count [B, C] int64, and
+ * (spec_cap non-NULL) the spec cap of each candidate
+ * (local_matcher.py:76-81). num_caps <= 16. */
+int sg_global_candidates(const int64_t* sa_len, const int64_t* sa_start,
+                         const int64_t* sa_end, const int64_t* d_len,
+                         const int64_t* d_pos, const int64_t* d_cnt,
+                         const int32_t* sa, const int32_t* corpus,
+                         int64_t capacity, const int32_t* delta,
+                         int64_t delta_capacity, const int64_t* delta_len,
+                         int32_t batch, int32_t num_caps, int32_t max_occ,
+                         int32_t k, int32_t has_spec_factor,
+                         float spec_factor, float spec_offset,
+                         int64_t* match_len, int32_t* cont,
+                         int64_t* occ_count, int64_t* spec_cap,
+                         sg_stream_t stream);
+
+/* Final selection of SuffixGPUDrafter.propose (proposer.py:305-331): per
+ * row, the first-maximum global candidate replaces the local draft (already
+ * in draft / num_valid, as written by sg_local_draft) when its score is
+ * strictly greater than local_score and the row may draft. */
+int sg_global_combine(int32_t* draft, int32_t* num_valid,
+                      const float* local_score, const uint8_t* row_mask,
+                      const int32_t* g_chain, const int64_t* g_emit,
+                      const float* g_score, int32_t batch, int32_t num_caps,
+                      int32_t k, sg_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -74,6 +74,29 @@ _SIGS: dict[str, list] = {
     "sg_expand_chain": [c_void_p, c_int32, c_int32, c_int32, c_void_p,
                         c_void_p, c_float, c_float, c_void_p, c_void_p,
                         c_void_p, c_void_p, c_void_p],
+    "sg_build_suffix_array": [c_void_p, c_int64, c_void_p, c_void_p,
+                              c_size_t, POINTER(c_int32), c_void_p],
+    "sg_sa_search": [c_void_p, c_void_p, c_int64, c_void_p, c_int32, c_int32,
+                     c_void_p, c_void_p, c_void_p, c_void_p],
+    "sg_suffix_match_backoff": [c_void_p, c_void_p, c_int64, c_void_p,
+                                c_int32, c_int32, c_void_p, c_int32,
+                                c_void_p, c_int32, c_void_p, c_void_p,
+                                c_void_p, c_void_p, c_void_p],
+    "sg_delta_match_backoff": [c_void_p, c_int64, c_void_p, c_void_p,
+                               c_int32, c_int32, c_void_p, c_int32, c_void_p,
+                               c_int32, c_int32, c_void_p, c_void_p,
+                               c_void_p, c_void_p, c_void_p],
+    "sg_gather_tails": [c_void_p, c_int64, c_int32, c_void_p, c_int32,
+                        c_int32, c_void_p, c_void_p, c_void_p],
+    "sg_global_candidates": [c_void_p, c_void_p, c_void_p, c_void_p,
+                             c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                             c_void_p, c_int64, c_void_p, c_int32, c_int32,
+                             c_int32, c_int32, c_int32, c_float, c_float,
+                             c_void_p, c_void_p, c_void_p, c_void_p,
+                             c_void_p],
+    "sg_global_combine": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                          c_void_p, c_void_p, c_int32, c_int32, c_int32,
+                          c_void_p],
 }
 
 
@@ -102,7 +125,9 @@ def lib() -> ctypes.CDLL:
 
 
 # entry points with non-int return types: name -> (restype, argtypes)
-_SIGS_EXTRA: dict[str, tuple] = {}
+_SIGS_EXTRA: dict[str, tuple] = {
+    "sg_suffix_array_workspace_size": (c_size_t, [c_int64]),
+}
 
 
 def register(name: str, argtypes: list, restype=c_int) -> None:

@@ -1,0 +1,533 @@
+// Suffix-array construction for sm_100a: prefix doubling over the still
+// tied suffixes, each round sorted with a hand-written stable LSD radix
+// sort.
+//
+// Result: identical to suffix_gpu/suffix_array.py:15-63 (the suffix array
+// is unique: suffixes at distinct positions differ, end of string sorts
+// first). The reference re-sorts all n packed (rank, rank[i+k]) keys with
+// torch.argsort for ceil(log2 n) rounds; here
+//   * ranks are group starts (the SA index of the first suffix of each
+//     group of equal 2^r-prefixes), so a suffix whose group has one member
+//     is final and leaves the active set (Larsson-Sadakane doubling);
+//   * a round sorts only the active suffixes by the packed key
+//     (group start << SB) | (i + h < n ? rank[i + h] + 1 : 0);
+//     group starts are contiguous in SA order, so the sorted active list
+//     maps one-to-one onto the active SA slots;
+//   * one scan pass then writes SA entries, new group-start ranks and the
+//     next active list; the build stops when no group is left (no fixed
+//     round count).
+// Radix sort: 8-bit digits; per 4096-key tile a digit histogram, a
+// per-digit scan over tiles, and a stable scatter that ranks each 32-key
+// warp round with 8 ballots (no __match_any_sync, which is slow on
+// sm_100a).
+#include <cuda_runtime.h>
+
+#include "sg_common.cuh"
+
+namespace sg {
+
+constexpr int kSortThreads = 256;
+constexpr int kSortWarps = kSortThreads / 32;
+constexpr int kSortItems = 16;                    // keys per thread
+constexpr int kTile = kSortThreads * kSortItems;  // 4096 keys per tile
+
+// ---------------------------------------------------------------------------
+// radix sort passes
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kSortThreads)
+    rs_hist_kernel(const uint64_t* __restrict__ keys, int64_t m, int shift,
+                   uint32_t* __restrict__ tile_hist, int ntiles,
+                   uint32_t* __restrict__ totals) {
+  __shared__ uint32_t h[kSortWarps][256];
+  const int t = threadIdx.x, warp = warp_id();
+  for (int i = t; i < kSortWarps * 256; i += kSortThreads) (&h[0][0])[i] = 0;
+  __syncthreads();
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kTile;
+#pragma unroll
+  for (int r = 0; r < kSortItems; ++r) {
+    const int64_t idx = base + r * kSortThreads + t;
+    if (idx < m) atomicAdd(&h[warp][(keys[idx] >> shift) & 255], 1u);
+  }
+  __syncthreads();
+  uint32_t s = 0;
+#pragma unroll
+  for (int w = 0; w < kSortWarps; ++w) s += h[w][t];
+  tile_hist[static_cast<int64_t>(t) * ntiles + blockIdx.x] = s;
+  if (s) atomicAdd(&totals[t], s);
+}
+
+// Block d: exclusive scan of digit d's per-tile counts, offset by the
+// number of keys with a smaller digit.
+__global__ void __launch_bounds__(kSortThreads)
+    rs_scan_kernel(uint32_t* __restrict__ tile_hist, int ntiles,
+                   const uint32_t* __restrict__ totals) {
+  __shared__ uint32_t warp_sums[kSortWarps];
+  const int d = blockIdx.x, t = threadIdx.x;
+  const int warp = warp_id(), lane = lane_id();
+  // digit start = sum of totals[0..d)
+  uint32_t v = t < d ? totals[t] : 0u;
+  v = __reduce_add_sync(SG_FULL_MASK, v);
+  if (lane == 0) warp_sums[warp] = v;
+  __syncthreads();
+  uint32_t carry = 0;
+#pragma unroll
+  for (int w = 0; w < kSortWarps; ++w) carry += warp_sums[w];
+  __syncthreads();
+  uint32_t* row = tile_hist + static_cast<int64_t>(d) * ntiles;
+  for (int c0 = 0; c0 < ntiles; c0 += kSortThreads) {
+    const int i = c0 + t;
+    const uint32_t x = i < ntiles ? row[i] : 0u;
+    const uint32_t inc =
+        static_cast<uint32_t>(warp_incl_scan(static_cast<int>(x)));
+    if (lane == 31) warp_sums[warp] = inc;
+    __syncthreads();
+    uint32_t pre = 0, tot = 0;
+#pragma unroll
+    for (int w = 0; w < kSortWarps; ++w) {
+      const uint32_t y = warp_sums[w];
+      if (w < warp) pre += y;
+      tot += y;
+    }
+    if (i < ntiles) row[i] = carry + pre + inc - x;
+    carry += tot;
+    __syncthreads();
+  }
+}
+
+__global__ void zero_u32_kernel(uint32_t* p, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = 0u;
+}
+
+__global__ void __launch_bounds__(kSortThreads)
+    rs_scatter_kernel(const uint64_t* __restrict__ kin,
+                      const uint32_t* __restrict__ vin,
+                      uint64_t* __restrict__ kout, uint32_t* __restrict__ vout,
+                      int64_t m, int shift,
+                      const uint32_t* __restrict__ offs, int ntiles) {
+  __shared__ uint32_t wcnt[kSortWarps][256];
+  __shared__ uint32_t s_off[256];
+  const int t = threadIdx.x, warp = warp_id(), lane = lane_id();
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int i = lane; i < 256; i += 32) wcnt[warp][i] = 0u;
+  s_off[t] = offs[static_cast<int64_t>(t) * ntiles + blockIdx.x];
+  // warp w owns keys [base, base + 512) of the tile, 32 per round in order
+  const int64_t base =
+      static_cast<int64_t>(blockIdx.x) * kTile + warp * (32 * kSortItems);
+  uint64_t key[kSortItems];
+  uint32_t val[kSortItems];
+  uint32_t loc[kSortItems];
+#pragma unroll
+  for (int r = 0; r < kSortItems; ++r) {
+    const int64_t idx = base + r * 32 + lane;
+    key[r] = idx < m ? kin[idx] : 0ull;
+    val[r] = idx < m ? vin[idx] : 0u;
+  }
+  __syncwarp();
+  // stable rank of every key among this warp's keys with the same digit
+#pragma unroll
+  for (int r = 0; r < kSortItems; ++r) {
+    const int64_t idx = base + r * 32 + lane;
+    const bool valid = idx < m;
+    const uint32_t d = static_cast<uint32_t>(key[r] >> shift) & 255u;
+    unsigned peers = __ballot_sync(SG_FULL_MASK, valid);
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      const unsigned bal =
+          __ballot_sync(SG_FULL_MASK, valid && ((d >> b) & 1u));
+      peers &= ((d >> b) & 1u) ? bal : ~bal;
+    }
+    const int leader = valid ? __ffs(peers) - 1 : lane;
+    uint32_t old = 0;
+    if (valid && lane == leader) {
+      old = wcnt[warp][d];
+      wcnt[warp][d] = old + __popc(peers);
+    }
+    old = __shfl_sync(SG_FULL_MASK, old, leader);
+    loc[r] = old + __popc(peers & lt_mask);
+    __syncwarp();
+  }
+  __syncthreads();
+  // exclusive prefix over warps, per digit (thread t = digit t)
+  {
+    uint32_t run = 0;
+#pragma unroll
+    for (int w = 0; w < kSortWarps; ++w) {
+      const uint32_t c = wcnt[w][t];
+      wcnt[w][t] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < kSortItems; ++r) {
+    const int64_t idx = base + r * 32 + lane;
+    if (idx < m) {
+      const uint32_t d = static_cast<uint32_t>(key[r] >> shift) & 255u;
+      const uint32_t pos = s_off[d] + wcnt[warp][d] + loc[r];
+      kout[pos] = key[r];
+      vout[pos] = val[r];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// doubling rounds
+// ---------------------------------------------------------------------------
+constexpr int kScanThreads = 256;
+constexpr int kScanItems = 16;
+constexpr int kScanBlock = kScanThreads * kScanItems;
+
+__global__ void init_keys_kernel(const int32_t* __restrict__ tok, int64_t n,
+                                 uint64_t* __restrict__ keys,
+                                 uint32_t* __restrict__ vals) {
+  const int64_t i =
+      static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) {
+    // order-preserving map of signed int32 to unsigned
+    keys[i] = static_cast<uint32_t>(tok[i]) ^ 0x80000000u;
+    vals[i] = static_cast<uint32_t>(i);
+  }
+}
+
+__global__ void make_keys_kernel(const uint32_t* __restrict__ act,
+                                 const int32_t* __restrict__ sa,
+                                 const uint32_t* __restrict__ rank, int64_t n,
+                                 int64_t m, int64_t h, int sb,
+                                 uint64_t* __restrict__ keys,
+                                 uint32_t* __restrict__ vals) {
+  const int64_t t =
+      static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= m) return;
+  const int64_t i = sa[act[t]];
+  const uint64_t second =
+      i + h < n ? static_cast<uint64_t>(rank[i + h]) + 1 : 0;
+  keys[t] = (static_cast<uint64_t>(rank[i]) << sb) | second;
+  vals[t] = static_cast<uint32_t>(i);
+}
+
+// Element t of the sorted active list: head of a new group? still tied?
+__device__ __forceinline__ void round_flags(const uint64_t* K, int64_t m,
+                                            int64_t t, bool& head,
+                                            bool& keep) {
+  const uint64_t k = K[t];
+  head = (t == 0) || K[t - 1] != k;
+  const bool next_head = (t == m - 1) || K[t + 1] != k;
+  keep = !(head && next_head);
+}
+
+// Per scan block: max of the new group starts and count of elements that
+// stay active.
+__global__ void __launch_bounds__(kScanThreads)
+    round_reduce_kernel(const uint64_t* __restrict__ K,
+                        const uint32_t* __restrict__ act, int64_t m,
+                        uint32_t* __restrict__ blk_max,
+                        uint32_t* __restrict__ blk_sum) {
+  __shared__ uint32_t sm[kSortWarps], ss[kSortWarps];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanBlock;
+  uint32_t mx = 0, sum = 0;
+  for (int r = 0; r < kScanItems; ++r) {
+    const int64_t t = base + r * kScanThreads + threadIdx.x;
+    if (t < m) {
+      bool head, keep;
+      round_flags(K, m, t, head, keep);
+      const uint32_t a = act ? act[t] : static_cast<uint32_t>(t);
+      if (head) mx = max(mx, a);
+      sum += keep;
+    }
+  }
+  mx = __reduce_max_sync(SG_FULL_MASK, mx);
+  sum = __reduce_add_sync(SG_FULL_MASK, sum);
+  if (lane_id() == 0) {
+    sm[warp_id()] = mx;
+    ss[warp_id()] = sum;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t a = 0, b = 0;
+    for (int w = 0; w < kSortWarps; ++w) {
+      a = max(a, sm[w]);
+      b += ss[w];
+    }
+    blk_max[blockIdx.x] = a;
+    blk_sum[blockIdx.x] = b;
+  }
+}
+
+// Exclusive max-scan and sum-scan of the block aggregates (one block of
+// 1024 threads); writes the next active count.
+__global__ void __launch_bounds__(1024)
+    round_scan_blocks_kernel(uint32_t* blk_max, uint32_t* blk_sum, int nblk,
+                             int64_t* next_m) {
+  __shared__ uint32_t wm[32], ws[32];
+  __shared__ uint32_t carry_m, carry_s;
+  const int lane = lane_id(), warp = warp_id();
+  if (threadIdx.x == 0) {
+    carry_m = 0;
+    carry_s = 0;
+  }
+  __syncthreads();
+  for (int c0 = 0; c0 < nblk; c0 += 1024) {
+    const int i = c0 + threadIdx.x;
+    const uint32_t xm = i < nblk ? blk_max[i] : 0u;
+    const uint32_t xs = i < nblk ? blk_sum[i] : 0u;
+    uint32_t im = xm, is = xs;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t a = __shfl_up_sync(SG_FULL_MASK, im, o);
+      const uint32_t b = __shfl_up_sync(SG_FULL_MASK, is, o);
+      if (lane >= o) {
+        im = max(im, a);
+        is += b;
+      }
+    }
+    uint32_t em = __shfl_up_sync(SG_FULL_MASK, im, 1);
+    if (lane == 0) em = 0;
+    const uint32_t es = is - xs;
+    if (lane == 31) {
+      wm[warp] = im;
+      ws[warp] = is;
+    }
+    __syncthreads();
+    uint32_t pm = carry_m, ps = carry_s;
+    for (int w = 0; w < warp; ++w) {
+      pm = max(pm, wm[w]);
+      ps += ws[w];
+    }
+    if (i < nblk) {
+      blk_max[i] = max(pm, em);
+      blk_sum[i] = ps + es;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t a = carry_m, b = carry_s;
+      for (int w = 0; w < 32; ++w) {
+        a = max(a, wm[w]);
+        b += ws[w];
+      }
+      carry_m = a;
+      carry_s = b;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *next_m = carry_s;
+}
+
+// Writes sa[act[t]] = V[t], rank[V[t]] = start of t's group (the act value
+// of its group's first element: act is increasing, so a max-scan over
+// head-marked act values finds it) and compacts the still-tied elements
+// into act_next, all in element order.
+__global__ void __launch_bounds__(kScanThreads)
+    round_apply_kernel(const uint64_t* __restrict__ K,
+                       const uint32_t* __restrict__ V,
+                       const uint32_t* __restrict__ act, int64_t m,
+                       const uint32_t* __restrict__ blk_max,
+                       const uint32_t* __restrict__ blk_sum,
+                       int32_t* __restrict__ sa, uint32_t* __restrict__ rank,
+                       uint32_t* __restrict__ act_next) {
+  __shared__ uint32_t wm[kSortWarps], ws[kSortWarps];
+  const int lane = lane_id(), warp = warp_id();
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanBlock;
+  uint32_t carry_m = blk_max[blockIdx.x];
+  uint32_t carry_s = blk_sum[blockIdx.x];
+  for (int r = 0; r < kScanItems; ++r) {
+    const int64_t t = base + r * kScanThreads + threadIdx.x;
+    bool head = false, keep = false;
+    uint32_t a = 0;
+    if (t < m) {
+      round_flags(K, m, t, head, keep);
+      a = act ? act[t] : static_cast<uint32_t>(t);
+    }
+    uint32_t im = head ? a : 0u, is = keep ? 1u : 0u;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t x = __shfl_up_sync(SG_FULL_MASK, im, o);
+      const uint32_t y = __shfl_up_sync(SG_FULL_MASK, is, o);
+      if (lane >= o) {
+        im = max(im, x);
+        is += y;
+      }
+    }
+    if (lane == 31) {
+      wm[warp] = im;
+      ws[warp] = is;
+    }
+    __syncthreads();
+    uint32_t pm = carry_m, ps = carry_s, tm = carry_m, ts = carry_s;
+#pragma unroll
+    for (int w = 0; w < kSortWarps; ++w) {
+      if (w < warp) {
+        pm = max(pm, wm[w]);
+        ps += ws[w];
+      }
+      tm = max(tm, wm[w]);
+      ts += ws[w];
+    }
+    if (t < m) {
+      const uint32_t v = V[t];
+      sa[a] = static_cast<int32_t>(v);
+      rank[v] = max(pm, im);
+      if (keep) act_next[ps + is - 1] = a;
+    }
+    carry_m = tm;
+    carry_s = ts;
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host driver
+// ---------------------------------------------------------------------------
+static int bitlen(uint64_t x) {
+  int b = 0;
+  while (x) {
+    ++b;
+    x >>= 1;
+  }
+  return b;
+}
+
+struct SaWorkspace {
+  uint64_t* K[2];
+  uint32_t* V[2];
+  uint32_t* rank;
+  uint32_t* act[2];
+  uint32_t* tile_hist;
+  uint32_t* totals;
+  uint32_t* blk_max;
+  uint32_t* blk_sum;
+  int64_t* m_dev;
+  size_t bytes;
+};
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+static SaWorkspace carve(void* base, int64_t n) {
+  SaWorkspace w{};
+  const size_t un = static_cast<size_t>(n > 0 ? n : 1);
+  const size_t ntiles = (un + kTile - 1) / kTile;
+  const size_t nblk = (un + kScanBlock - 1) / kScanBlock;
+  char* p = static_cast<char*>(base);
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    char* r = p ? p + o : nullptr;
+    o = align256(o + bytes);
+    return r;
+  };
+  w.K[0] = reinterpret_cast<uint64_t*>(take(8 * un));
+  w.K[1] = reinterpret_cast<uint64_t*>(take(8 * un));
+  w.V[0] = reinterpret_cast<uint32_t*>(take(4 * un));
+  w.V[1] = reinterpret_cast<uint32_t*>(take(4 * un));
+  w.rank = reinterpret_cast<uint32_t*>(take(4 * un));
+  w.act[0] = reinterpret_cast<uint32_t*>(take(4 * un));
+  w.act[1] = reinterpret_cast<uint32_t*>(take(4 * un));
+  w.tile_hist = reinterpret_cast<uint32_t*>(take(4 * 256 * ntiles));
+  w.totals = reinterpret_cast<uint32_t*>(take(4 * 256));
+  w.blk_max = reinterpret_cast<uint32_t*>(take(4 * nblk));
+  w.blk_sum = reinterpret_cast<uint32_t*>(take(4 * nblk));
+  w.m_dev = reinterpret_cast<int64_t*>(take(8));
+  w.bytes = o;
+  return w;
+}
+
+// Stable LSD sort of (K[cur], V[cur]) by the low `bits` bits; returns the
+// buffer index holding the result.
+static int radix_sort(SaWorkspace& w, int cur, int64_t m, int bits,
+                      cudaStream_t st) {
+  const int ntiles = static_cast<int>((m + kTile - 1) / kTile);
+  for (int shift = 0; shift < bits; shift += 8) {
+    zero_u32_kernel<<<1, 256, 0, st>>>(w.totals, 256);
+    rs_hist_kernel<<<ntiles, kSortThreads, 0, st>>>(
+        w.K[cur], m, shift, w.tile_hist, ntiles, w.totals);
+    rs_scan_kernel<<<256, kSortThreads, 0, st>>>(w.tile_hist, ntiles,
+                                                 w.totals);
+    rs_scatter_kernel<<<ntiles, kSortThreads, 0, st>>>(
+        w.K[cur], w.V[cur], w.K[1 - cur], w.V[1 - cur], m, shift,
+        w.tile_hist, ntiles);
+    cur = 1 - cur;
+  }
+  return cur;
+}
+
+// One apply pass; returns the next active count (host sync).
+static int apply_round(SaWorkspace& w, int kcur, const uint32_t* act,
+                       uint32_t* act_next, int64_t m, int32_t* sa,
+                       cudaStream_t st, int64_t* next_m, int* err) {
+  const int nblk = static_cast<int>((m + kScanBlock - 1) / kScanBlock);
+  round_reduce_kernel<<<nblk, kScanThreads, 0, st>>>(w.K[kcur], act, m,
+                                                    w.blk_max, w.blk_sum);
+  round_scan_blocks_kernel<<<1, 1024, 0, st>>>(w.blk_max, w.blk_sum, nblk,
+                                               w.m_dev);
+  round_apply_kernel<<<nblk, kScanThreads, 0, st>>>(
+      w.K[kcur], w.V[kcur], act, m, w.blk_max, w.blk_sum, sa, w.rank,
+      act_next);
+  cudaError_t e = cudaMemcpyAsync(next_m, w.m_dev, sizeof(int64_t),
+                                  cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    *err = SG_ERR_CUDA;
+    return 0;
+  }
+  return 1;
+}
+
+}  // namespace sg
+
+using namespace sg;
+
+extern "C" size_t sg_suffix_array_workspace_size(int64_t n) {
+  if (n < 0) return 0;
+  return carve(nullptr, n).bytes;
+}
+
+extern "C" int sg_build_suffix_array(const int32_t* tokens, int64_t n,
+                                     int32_t* sa_out, void* workspace,
+                                     size_t ws_bytes, int32_t* rounds_out,
+                                     sg_stream_t stream) {
+  if (n < 0) return SG_ERR_INVALID;
+  if (n >= (int64_t(1) << 31) - 1) return SG_ERR_UNSUPPORTED;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (rounds_out) *rounds_out = 0;
+  if (n == 0) return SG_OK;
+  if (!tokens || !sa_out) return SG_ERR_INVALID;
+  if (n == 1) {
+    cudaError_t e = cudaMemsetAsync(sa_out, 0, sizeof(int32_t), st);
+    if (e != cudaSuccess) {
+      set_cuda_error(e);
+      return SG_ERR_CUDA;
+    }
+    return SG_OK;
+  }
+  if (!workspace || ws_bytes < carve(nullptr, n).bytes)
+    return SG_ERR_WORKSPACE;
+  SaWorkspace w = carve(workspace, n);
+
+  // round 0: sort by the first token
+  init_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(
+      tokens, n, w.K[0], w.V[0]);
+  int kcur = radix_sort(w, 0, n, 32, st);
+  int err = SG_OK;
+  int64_t m = 0;
+  int acur = 0;
+  if (!apply_round(w, kcur, nullptr, w.act[acur], n, sa_out, st, &m, &err))
+    return err;
+  const int sb = bitlen(static_cast<uint64_t>(n));        // rank[i+h]+1 <= n
+  const int pb = bitlen(static_cast<uint64_t>(n - 1));    // group start < n
+  int rounds = 0;
+  for (int64_t h = 1; m > 0; h <<= 1) {
+    if (h >= n) return SG_ERR_CUDA;  // cannot happen for a correct build
+    make_keys_kernel<<<static_cast<unsigned>((m + 255) / 256), 256, 0, st>>>(
+        w.act[acur], sa_out, w.rank, n, m, h, sb, w.K[0], w.V[0]);
+    kcur = radix_sort(w, 0, m, pb + sb, st);
+    int64_t m_next = 0;
+    if (!apply_round(w, kcur, w.act[acur], w.act[1 - acur], m, sa_out, st,
+                     &m_next, &err))
+      return err;
+    acur = 1 - acur;
+    m = m_next;
+    ++rounds;
+  }
+  if (rounds_out) *rounds_out = rounds;
+  return check_launch();
+}

@@ -1,0 +1,436 @@
+"""GlobalIndex: cross-request memory (suffix array over finished responses
+plus an append-only delta buffer), the reference's GlobalIndex
+(suffix_gpu/global_index.py:41-553) on the sm_100a kernels.
+
+The host-side bookkeeping (document lengths, eviction, snapshot, delta
+compaction, rebuild trigger and swap) follows the reference step by step;
+the device work goes through the C ABI: sg_build_suffix_array for the
+staging SA, sg_suffix_match_backoff + sg_delta_match_backoff +
+sg_global_candidates for queries. The active corpus/SA keep their storage
+across swaps (in-place copies), so captured CUDA graphs stay valid.
+
+Rebuilds run synchronously (the reference's behaviour on CPU and without a
+rebuild stream). With ``rebuild_stream`` set, the staging build runs on
+that stream from a background host thread and the swap happens at the
+first ``poll_rebuild`` after it has finished, as in the reference.
+"""
+
+from __future__ import annotations
+
+import threading
+from collections import deque
+
+import torch
+
+from suffixgpu_b200 import ops
+from suffixgpu_b200._lib import call, ptr, stream_of
+
+PAD_TOKEN = torch.iinfo(torch.int32).max
+SEP_TOKEN = -2
+
+
+class _ThreadEvent:
+    """Completion flag of a background build (query() like a CUDA event)."""
+
+    def __init__(self):
+        self._done = threading.Event()
+        self.error: BaseException | None = None
+
+    def set(self):
+        self._done.set()
+
+    def query(self) -> bool:
+        return self._done.is_set()
+
+    def wait(self):
+        self._done.wait()
+
+
+class GlobalIndex:
+    """GPU-resident global suffix index with periodic rebuilds."""
+
+    def __init__(self, capacity: int, delta_capacity: int, k: int,
+                 max_occurrences: int = 32,
+                 rebuild_threshold: int | None = None,
+                 device: torch.device | str = "cuda",
+                 rebuild_stream: torch.cuda.Stream | None = None):
+        self.capacity = capacity
+        self.delta_capacity = delta_capacity
+        self.k = k
+        self.max_occurrences = max_occurrences
+        self.rebuild_threshold = rebuild_threshold or max(
+            1, delta_capacity // 2)
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("GlobalIndex (suffixgpu_b200) needs a CUDA "
+                             "device")
+        self.rebuild_stream = rebuild_stream
+        dev = self.device
+        self.corpus = torch.full((capacity,), PAD_TOKEN, dtype=torch.int32,
+                                 device=dev)
+        self.staging_corpus = self.corpus.clone()
+        self.sa = torch.arange(capacity, dtype=torch.int32, device=dev)
+        self.staging_sa = self.sa.clone()
+        self._arange = self.sa.clone()
+        self.delta = torch.zeros(delta_capacity, dtype=torch.int32,
+                                 device=dev)
+        self.delta_len_t = torch.zeros((), dtype=torch.int64, device=dev)
+        self.active_len = 0
+        self.delta_len = 0
+        self.active_doc_lens: deque[int] = deque()
+        self.delta_doc_lens: list[int] = []
+        self._rebuild_event = None
+        self._pending = None
+        self._worker: threading.Thread | None = None
+        self.rebuilds = 0
+        self.last_rounds = 0
+        self._sa_ws: torch.Tensor | None = None
+
+    # ------------------------------------------------------------------
+    # writes (global_index.py:86-133)
+    # ------------------------------------------------------------------
+    def append_documents(self, docs: list[torch.Tensor]) -> None:
+        """Append finished-response token tensors to the delta, each
+        followed by one SEP_TOKEN (recorded doc lengths include it)."""
+        for doc in docs:
+            doc = doc.to(self.device).to(torch.int32).reshape(-1)
+            n = doc.shape[0]
+            if n == 0:
+                continue
+            if n + 1 > self.delta_capacity:
+                doc = doc[-(self.delta_capacity - 1):]
+                n = doc.shape[0]
+            if self.delta_len + n + 1 > self.delta_capacity:
+                self._make_room(n + 1)
+            self.delta[self.delta_len:self.delta_len + n].copy_(doc)
+            self.delta[self.delta_len + n] = SEP_TOKEN
+            self.delta_len += n + 1
+            self.delta_len_t.fill_(self.delta_len)
+            self.delta_doc_lens.append(n + 1)
+        self.maybe_rebuild()
+
+    def _make_room(self, needed: int) -> None:
+        self.poll_rebuild()
+        if self._rebuild_event is None:
+            self._launch_rebuild()
+        if self.delta_len + needed <= self.delta_capacity:
+            return
+        # A rebuild is in flight (staging buffers busy): drop oldest docs.
+        self._drop_oldest_docs(self.delta_len + needed - self.delta_capacity)
+
+    def _drop_oldest_docs(self, drop: int) -> None:
+        acc = 0
+        docs_dropped = 0
+        for ln in self.delta_doc_lens:
+            if acc >= drop:
+                break
+            acc += ln
+            docs_dropped += 1
+        remaining = self.delta_len - acc
+        if remaining > 0:
+            self.delta[:remaining] = self.delta[acc:self.delta_len].clone()
+        self.delta_len = remaining
+        self.delta_len_t.fill_(remaining)
+        self.delta_doc_lens = self.delta_doc_lens[docs_dropped:]
+
+    # ------------------------------------------------------------------
+    # rebuild (global_index.py:138-253)
+    # ------------------------------------------------------------------
+    def maybe_rebuild(self) -> None:
+        """Kick off a rebuild when the delta grew past the threshold."""
+        self.poll_rebuild()
+        if self._rebuild_event is not None or self.delta_len == 0:
+            return
+        if self.delta_len < self.rebuild_threshold:
+            return
+        self._launch_rebuild()
+
+    def _launch_rebuild(self) -> None:
+        if self._rebuild_event is not None:
+            return
+        # Evict oldest whole docs until the snapshot fits into capacity.
+        keep_start = 0
+        for ln in self.active_doc_lens:
+            if self.active_len - keep_start + self.delta_len \
+                    <= self.capacity:
+                break
+            keep_start += ln
+        n_active_keep = self.active_len - keep_start
+        snap = min(self.delta_len, self.capacity - n_active_keep)
+        # Clamp the snapshot to a whole-doc boundary in the delta.
+        acc = 0
+        for ln in self.delta_doc_lens:
+            if acc + ln <= snap:
+                acc += ln
+            else:
+                break
+        snap = acc
+        n_new = n_active_keep + snap
+        if n_new == 0:
+            return
+
+        dst = self.staging_corpus
+        dst.fill_(PAD_TOKEN)
+        if n_active_keep > 0:
+            dst[:n_active_keep].copy_(
+                self.corpus[keep_start:self.active_len])
+        if snap > 0:
+            dst[n_active_keep:n_new].copy_(self.delta[:snap])
+
+        new_doc_lens: deque[int] = deque()
+        acc = 0
+        for ln in self.active_doc_lens:
+            acc += ln
+            if acc > keep_start:
+                new_doc_lens.append(ln)
+        acc = 0
+        for ln in self.delta_doc_lens:
+            acc += ln
+            if acc <= snap:
+                new_doc_lens.append(ln)
+
+        # Staging owns a copy of the snapshot; compact it out of the delta.
+        docs_absorbed = self._count_docs_within(snap)
+        remaining = self.delta_len - snap
+        if remaining > 0:
+            self.delta[:remaining] = self.delta[snap:self.delta_len].clone()
+        self.delta_len = remaining
+        self.delta_len_t.fill_(remaining)
+        self.delta_doc_lens = self.delta_doc_lens[docs_absorbed:]
+
+        # Build over the real prefix plus one sentinel column.
+        m = min(n_new + 1, self.capacity)
+        if self._sa_ws is None:
+            from suffixgpu_b200 import _lib
+            need = int(_lib.lib().sg_suffix_array_workspace_size(
+                self.capacity))
+            self._sa_ws = torch.empty(need, dtype=torch.uint8,
+                                      device=self.device)
+        if self.rebuild_stream is not None:
+            self.rebuild_stream.wait_stream(
+                torch.cuda.current_stream(self.device))
+            ev = _ThreadEvent()
+            self._pending = (n_new, new_doc_lens)
+            self._rebuild_event = ev
+
+            def work():
+                try:
+                    with torch.cuda.device(self.device):
+                        self._build_staging_sa(
+                            dst, m, self.rebuild_stream.cuda_stream)
+                except BaseException as e:  # surfaced at poll time
+                    ev.error = e
+                ev.set()
+
+            self._worker = threading.Thread(target=work, daemon=True)
+            self._worker.start()
+        else:
+            self._build_staging_sa(dst, m, None)
+            self._finish_swap(n_new, new_doc_lens)
+
+    def _build_staging_sa(self, dst: torch.Tensor, m: int,
+                          stream: int | None) -> None:
+        self.last_rounds = ops.build_suffix_array_into(
+            dst[:m], self.staging_sa[:m], workspace=self._sa_ws,
+            stream=stream)
+        if m < self.capacity:
+            # all-sentinel suffixes compare greater than any real pattern
+            if stream is None:
+                self.staging_sa[m:].copy_(self._arange[m:])
+            else:
+                with torch.cuda.stream(torch.cuda.ExternalStream(stream)):
+                    self.staging_sa[m:].copy_(self._arange[m:])
+                torch.cuda.ExternalStream(stream).synchronize()
+
+    def _count_docs_within(self, tokens: int) -> int:
+        acc = 0
+        count = 0
+        for ln in self.delta_doc_lens:
+            acc += ln
+            if acc > tokens:
+                break
+            count += 1
+        return count
+
+    def _finish_swap(self, n_new: int, new_doc_lens: deque[int]) -> None:
+        # In-place copies keep the active tensors' storage (graph safety).
+        self.corpus.copy_(self.staging_corpus)
+        self.sa.copy_(self.staging_sa)
+        self.active_len = n_new
+        self.active_doc_lens = new_doc_lens
+        self._rebuild_event = None
+        self._pending = None
+        self._worker = None
+        self.rebuilds += 1
+
+    def poll_rebuild(self) -> None:
+        """Swap in a finished background rebuild (non-blocking)."""
+        if self._rebuild_event is None:
+            return
+        if self._rebuild_event.query():
+            err = getattr(self._rebuild_event, "error", None)
+            if err is not None:
+                self._rebuild_event = None
+                self._pending = None
+                raise RuntimeError("background suffix-array build failed") \
+                    from err
+            n_new, new_doc_lens = self._pending
+            self._finish_swap(n_new, new_doc_lens)
+
+    def wait_rebuild(self) -> None:
+        """Block until an in-flight background rebuild has finished and
+        swap it in (deterministic schedules in tests)."""
+        if self._rebuild_event is None:
+            return
+        wait = getattr(self._rebuild_event, "wait", None)
+        if wait is not None:
+            wait()
+        self.poll_rebuild()
+
+    # ------------------------------------------------------------------
+    # queries (global_index.py:257-370, 443-553)
+    # ------------------------------------------------------------------
+    def query(self, query: torch.Tensor, query_len: torch.Tensor,
+              max_len: int):
+        """Longest-suffix match against corpus + delta: (match_len [B] i64,
+        cont [B, R, k] int32 (-1 padded), occ_count [B] i64)."""
+        caps = torch.full((1,), max_len, dtype=torch.int64,
+                          device=self.device)
+        ml, cont, occ = self._query_backoff(query, query_len, max_len, caps)
+        return ml[:, 0], cont[:, 0], occ[:, 0]
+
+    def _query_backoff(self, query, query_len, max_len: int, caps,
+                       row_mask=None, spec=None):
+        """Per-cap matches against corpus + delta: (match_len [B, C] i64,
+        cont [B, C, R, k] int32, occ_count [B, C] i64) and, with
+        spec=(has_factor, factor, offset), the spec caps [B, C] i64."""
+        dev = self.device
+        query = ops.as_i32(query)
+        query_len = ops.as_i64(query_len)
+        caps = ops.as_i64(caps)
+        b = query.shape[0]
+        cnum = caps.numel()
+        r = self.max_occurrences
+        sa_len, sa_start, sa_end = ops.suffix_match_backoff(
+            self.sa, self.corpus, query, query_len, max_len, caps,
+            row_mask=row_mask)
+        d_len, d_pos, d_cnt = self._delta_match_backoff(
+            query, query_len, max_len, caps, row_mask=row_mask)
+        match_len = torch.empty(b, cnum, dtype=torch.int64, device=dev)
+        cont = torch.empty(b, cnum, r, self.k, dtype=torch.int32, device=dev)
+        occ = torch.empty(b, cnum, dtype=torch.int64, device=dev)
+        cap_out = None
+        has_f, fac, off = 0, 0.0, 0.0
+        if spec is not None:
+            cap_out = torch.empty(b, cnum, dtype=torch.int64, device=dev)
+            has_f, fac, off = spec
+        call("sg_global_candidates", ptr(sa_len), ptr(sa_start), ptr(sa_end),
+             ptr(d_len), ptr(d_pos), ptr(d_cnt), ptr(self.sa),
+             ptr(self.corpus), self.capacity, ptr(self.delta),
+             self.delta_capacity, ptr(self.delta_len_t), b, cnum, r, self.k,
+             int(has_f), float(fac), float(off), ptr(match_len), ptr(cont),
+             ptr(occ), ptr(cap_out), stream_of(dev))
+        if spec is not None:
+            return match_len, cont, occ, cap_out
+        return match_len, cont, occ
+
+    def _delta_match_backoff(self, query, query_len, max_len: int, caps,
+                             row_mask=None):
+        """(match_len [B, C], start positions [B, C, R], count [B, C]),
+        int64 (global_index.py:465-546)."""
+        dev = self.device
+        query = ops.as_i32(query)
+        query_len = ops.as_i64(query_len)
+        caps = ops.as_i64(caps)
+        b, q = query.shape
+        cnum = caps.numel()
+        r = self.max_occurrences
+        lo = torch.empty(b, cnum, dtype=torch.int64, device=dev)
+        pos = torch.empty(b, cnum, r, dtype=torch.int64, device=dev)
+        cnt = torch.empty(b, cnum, dtype=torch.int64, device=dev)
+        rm = None if row_mask is None else row_mask.to(torch.bool).contiguous()
+        call("sg_delta_match_backoff", ptr(self.delta), self.delta_capacity,
+             ptr(self.delta_len_t), ptr(query), b, q, ptr(query_len),
+             max_len, ptr(caps), cnum, r, ptr(rm), ptr(lo), ptr(pos),
+             ptr(cnt), stream_of(dev))
+        return lo, pos, cnt
+
+    def draft(self, query, query_len, max_len: int, k: int,
+              min_token_prob: float = 0.0,
+              max_spec_factor: float | None = None,
+              max_spec_offset: float = 0.0, caps=None, alpha: float = 0.0):
+        """Multi-length scored draft over corpus + delta
+        (global_index.py:372-441): (chain [B, k] int32, num_valid [B] i64,
+        match_len [B] i64, occ_count [B] i64, score [B] f32)."""
+        dev = self.device
+        b = query.shape[0]
+        if caps is None:
+            caps = torch.tensor(
+                sorted({max_len, max(2, max_len // 2),
+                        max(2, max_len // 4), 2}, reverse=True),
+                dtype=torch.int64, device=dev)
+        cnum = caps.numel()
+        spec = (max_spec_factor is not None, max_spec_factor or 0.0,
+                max_spec_offset)
+        match_len, cont, occ, cap_emit = self._query_backoff(
+            query, query_len, max_len, caps, spec=spec)
+        if max_spec_factor is None:
+            cap_emit = torch.full_like(cap_emit, k)
+        chain, _, num_emit, score = ops.expand_chain(
+            cont.reshape(b * cnum, self.max_occurrences, self.k),
+            occ.reshape(b * cnum), k, min_token_prob=min_token_prob,
+            cap=cap_emit.reshape(-1), alpha=alpha)
+        score = score.reshape(b, cnum)
+        best = score.argmax(dim=1)
+        bidx = torch.arange(b, device=dev)
+        best_chain = chain.reshape(b, cnum, k)[bidx, best]
+        best_emit = num_emit.reshape(b, cnum)[bidx, best]
+        best_len = match_len[bidx, best]
+        best_occ = occ[bidx, best]
+        best_score = score[bidx, best]
+        slot = torch.arange(k, device=dev).unsqueeze(0)
+        best_chain = torch.where(slot < best_emit.unsqueeze(1), best_chain,
+                                 -1)
+        return best_chain, best_emit, best_len, best_occ, best_score
+
+    def expand(self, cont: torch.Tensor, occ_count: torch.Tensor,
+               min_token_prob: float = 0.0):
+        chain, num_valid, _, _ = ops.expand_chain(
+            cont, occ_count, self.k, min_token_prob=min_token_prob)
+        return chain, num_valid
+
+    # ------------------------------------------------------------------
+    # drafter step (proposer.py:246-320)
+    # ------------------------------------------------------------------
+    def propose_combine(self, counts: torch.Tensor, token_ids: torch.Tensor,
+                        local: dict, drafter) -> tuple[torch.Tensor,
+                                                       torch.Tensor]:
+        """Global candidates for the rows the local kernel just drafted,
+        expanded and scored, then combined with the local winner in place
+        (global wins only on a strictly greater score)."""
+        dev = self.device
+        b, s = token_ids.shape
+        p = drafter.max_pattern_len
+        counts = ops.as_i32(counts)
+        tails = torch.empty(b, p, dtype=torch.int32, device=dev)
+        tail_len = torch.empty(b, dtype=torch.int64, device=dev)
+        st = stream_of(dev)
+        call("sg_gather_tails", ptr(token_ids), token_ids.stride(0), s,
+             ptr(counts), b, p, ptr(tails), ptr(tail_len), st)
+        caps = drafter._global_caps
+        spec = (drafter.max_spec_factor is not None,
+                drafter.max_spec_factor or 0.0, drafter.max_spec_offset)
+        row_mask = local["row_mask"]
+        match_len, cont, occ, cap = self._query_backoff(
+            tails, tail_len, p, caps, row_mask=row_mask, spec=spec)
+        cnum = caps.numel()
+        chain, _, emit, score = ops.expand_chain(
+            cont.reshape(b * cnum, self.max_occurrences, self.k),
+            occ.reshape(-1), drafter.k,
+            min_token_prob=drafter.min_token_prob, cap=cap.reshape(-1),
+            alpha=drafter.vote_smoothing_alpha)
+        draft, nv = local["draft"], local["num_valid"]
+        call("sg_global_combine", ptr(draft), ptr(nv),
+             ptr(local["best_score"]), ptr(row_mask), ptr(chain), ptr(emit),
+             ptr(score), b, cnum, drafter.k, st)
+        return draft, nv

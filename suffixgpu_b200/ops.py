@@ -119,3 +119,97 @@ def expand_chain(cont: torch.Tensor, num_occ: torch.Tensor, k: int,
          float(min_token_prob), float(alpha), ptr(chain), ptr(nv),
          ptr(emit), ptr(score), stream_of(dev))
     return chain, nv, emit, score
+
+
+# ---------------------------------------------------------------------------
+# suffix array (suffix_gpu/suffix_array.py, sa_search.py)
+# ---------------------------------------------------------------------------
+_ws_cache: dict = {}
+
+
+def _workspace(device: torch.device, nbytes: int, tag: str) -> torch.Tensor:
+    """Cached per-device scratch buffer of at least nbytes."""
+    key = (device.index, tag)
+    buf = _ws_cache.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+        _ws_cache[key] = buf
+    return buf
+
+
+def build_suffix_array_into(tokens: torch.Tensor, out: torch.Tensor,
+                            workspace: torch.Tensor | None = None,
+                            stream: int | None = None) -> int:
+    """Suffix array of the 1-D int32 tokens into the int32 `out` (same
+    length). Returns the number of doubling rounds. Synchronises the
+    stream it runs on (once per round)."""
+    dev = require_cuda(tokens, out)
+    tokens = as_i32(tokens.reshape(-1))
+    n = tokens.numel()
+    if out.dtype != torch.int32 or out.numel() < n or not out.is_contiguous():
+        raise ValueError("out must be a contiguous int32 tensor of length n")
+    L = _lib.lib()
+    need = int(L.sg_suffix_array_workspace_size(n))
+    if workspace is None or workspace.numel() < need:
+        workspace = _workspace(dev, need, "sa")
+    rounds = _lib.c_int32(0)
+    call("sg_build_suffix_array", ptr(tokens), n, ptr(out), ptr(workspace),
+         workspace.numel(), _lib.ctypes.byref(rounds),
+         stream if stream is not None else stream_of(dev))
+    return int(rounds.value)
+
+
+def build_suffix_array(tokens: torch.Tensor) -> torch.Tensor:
+    """build_suffix_array (suffix_array.py:15-63): int64 start positions of
+    the suffixes in lexicographic order."""
+    dev = require_cuda(tokens)
+    n = tokens.numel()
+    out = torch.empty(n, dtype=torch.int32, device=dev)
+    if n:
+        build_suffix_array_into(tokens, out)
+    return out.to(torch.int64)
+
+
+def search_interval(sa: torch.Tensor, corpus: torch.Tensor,
+                    pattern: torch.Tensor, pattern_len: torch.Tensor):
+    """search_interval (sa_search.py:66-107): SA interval [start, end) of
+    the suffixes starting with each pattern. Returns (start, end) int64."""
+    dev = require_cuda(sa, corpus, pattern, pattern_len)
+    sa = as_i32(sa)
+    corpus = as_i32(corpus)
+    pattern = as_i32(pattern)
+    plen = as_i64(pattern_len)
+    b, m = pattern.shape
+    start = torch.empty(b, dtype=torch.int64, device=dev)
+    end = torch.empty(b, dtype=torch.int64, device=dev)
+    call("sg_sa_search", ptr(sa), ptr(corpus), sa.numel(), ptr(pattern), b,
+         m, ptr(plen), ptr(start), ptr(end), stream_of(dev))
+    return start, end
+
+
+def suffix_match_backoff(sa, corpus, query, query_len, max_len: int, caps,
+                         row_mask=None):
+    """suffix_match_backoff (sa_search.py:110-163). Returns (match_len,
+    start, end), each [B, C] int64."""
+    dev = require_cuda(sa, corpus, query, query_len, caps)
+    sa = as_i32(sa)
+    corpus = as_i32(corpus)
+    query = as_i32(query)
+    qlen = as_i64(query_len)
+    caps = as_i64(caps)
+    b, q = query.shape
+    c = caps.numel()
+    out = [torch.empty(b, c, dtype=torch.int64, device=dev) for _ in range(3)]
+    rm = None if row_mask is None else row_mask.to(torch.bool).contiguous()
+    call("sg_suffix_match_backoff", ptr(sa), ptr(corpus), sa.numel(),
+         ptr(query), b, q, ptr(qlen), max_len, ptr(caps), c, ptr(rm),
+         ptr(out[0]), ptr(out[1]), ptr(out[2]), stream_of(dev))
+    return out[0], out[1], out[2]
+
+
+def longest_suffix_match(sa, corpus, query, query_len, max_len: int):
+    """longest_suffix_match (sa_search.py:166-185)."""
+    caps = torch.full((1,), max_len, dtype=torch.int64, device=sa.device)
+    best, s, e = suffix_match_backoff(sa, corpus, query, query_len, max_len,
+                                      caps)
+    return best[:, 0], s[:, 0], e[:, 0]

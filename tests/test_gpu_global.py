@@ -1,0 +1,278 @@
+"""GPU parity of the suffix-array build, the SA search, the delta scan and
+the global drafter path against the reference goldens and the oracle.
+Bit-exact (integer outputs; scores compared as fp32 bit patterns)."""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import scenarios
+from oracle import suffix_oracle as so
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def _host(t):
+    return t.detach().cpu().numpy().copy()
+
+
+# ---------------------------------------------------------------------------
+# suffix array
+# ---------------------------------------------------------------------------
+def test_suffix_array_goldens(golden_dir):
+    from suffixgpu_b200 import ops
+    z = np.load(os.path.join(golden_dir, "sa_cases.npz"))
+    for i in range(int(z["n"])):
+        sa = ops.build_suffix_array(_dev(z[f"t{i}"]))
+        np.testing.assert_array_equal(_host(sa), z[f"sa{i}"], f"case {i}")
+
+
+@pytest.mark.parametrize("n,vocab", [(2, 1), (3, 2), (31, 3), (64, 8),
+                                     (200, 16), (1000, 2), (5000, 3),
+                                     (70000, 50000), (300000, 4)])
+def test_suffix_array_random_vs_oracle(n, vocab):
+    from suffixgpu_b200 import ops
+    rng = np.random.default_rng(n + vocab)
+    tok = rng.integers(-3, vocab, size=n).astype(np.int32)
+    got = _host(ops.build_suffix_array(_dev(tok)))
+    np.testing.assert_array_equal(got, so.build_suffix_array(tok))
+
+
+def test_suffix_array_edge_tokens():
+    """PAD (int32 max), SEP (-2), int32 min, long runs, empty and single."""
+    from suffixgpu_b200 import ops
+    t = np.array([2 ** 31 - 1] * 7 + [-2, 5, -2, -(2 ** 31), 0, 0, 0] * 3,
+                 dtype=np.int32)
+    np.testing.assert_array_equal(_host(ops.build_suffix_array(_dev(t))),
+                                  so.build_suffix_array(t))
+    run = np.full(4097, 9, dtype=np.int32)
+    np.testing.assert_array_equal(_host(ops.build_suffix_array(_dev(run))),
+                                  so.build_suffix_array(run))
+    assert ops.build_suffix_array(_dev(np.zeros(0, np.int32))).numel() == 0
+    assert _host(ops.build_suffix_array(_dev(np.array([7], np.int32)))) \
+        .tolist() == [0]
+
+
+def _sa_is_sorted(tok: np.ndarray, sa: np.ndarray) -> None:
+    """Linear-time certificate that sa is the suffix array of tok: a
+    permutation, and consecutive suffixes ordered by (token, rank of the
+    next suffix) with the end of string smallest."""
+    n = tok.shape[0]
+    assert np.array_equal(np.sort(sa), np.arange(n))
+    rank = np.empty(n + 1, dtype=np.int64)
+    rank[sa] = np.arange(n)
+    rank[n] = -1
+    a, b = sa[:-1], sa[1:]
+    ta, tb = tok[a].astype(np.int64), tok[b].astype(np.int64)
+    ok = (ta < tb) | ((ta == tb) & (rank[a + 1] < rank[b + 1]))
+    assert ok.all(), f"{(~ok).sum()} unsorted neighbours"
+
+
+def test_suffix_array_config4_size_property():
+    """BASELINE config 4 at full size (2^24 tokens, 50% copies): checked by
+    the linear-time sortedness certificate."""
+    from suffixgpu_b200 import ops
+    from suffixgpu_b200 import workloads as wl
+    tok = wl.config4(n=1 << 24, n_queries=1)["tokens"]
+    sa = _host(ops.build_suffix_array(_dev(tok)))
+    _sa_is_sorted(tok, sa)
+
+
+def test_suffix_array_config4_shape_vs_oracle():
+    from suffixgpu_b200 import ops
+    from suffixgpu_b200 import workloads as wl
+    tok = wl.config4(seed=9, n=1 << 18, n_queries=1)["tokens"]
+    np.testing.assert_array_equal(_host(ops.build_suffix_array(_dev(tok))),
+                                  so.build_suffix_array(tok))
+
+
+# ---------------------------------------------------------------------------
+# SA search
+# ---------------------------------------------------------------------------
+def test_sa_search_goldens(golden_dir):
+    from suffixgpu_b200 import ops
+    z = np.load(os.path.join(golden_dir, "sa_search_cases.npz"))
+    s, e = ops.search_interval(_dev(z["sa"]), _dev(z["corpus"]),
+                               _dev(z["pat"]), _dev(z["plen"]))
+    np.testing.assert_array_equal(_host(s), z["start"])
+    np.testing.assert_array_equal(_host(e), z["end"])
+    ml, bs, be = ops.suffix_match_backoff(
+        _dev(z["sa"]), _dev(z["corpus"]), _dev(z["q"]), _dev(z["qlen"]), 12,
+        _dev(z["caps"]))
+    np.testing.assert_array_equal(_host(ml), z["b_len"])
+    np.testing.assert_array_equal(_host(bs), z["b_start"])
+    np.testing.assert_array_equal(_host(be), z["b_end"])
+
+
+def test_sa_search_random_vs_oracle():
+    """Random corpora incl. PAD tails, patterns longer than the width and
+    negative / zero lengths (the comparator's clamped column rule)."""
+    from suffixgpu_b200 import ops
+    rng = np.random.default_rng(5)
+    for trial in range(4):
+        n = int(rng.integers(50, 3000))
+        corpus = rng.integers(0, 4, size=n).astype(np.int32)
+        corpus[-int(rng.integers(0, 10)):] = so.PAD_TOKEN
+        sa = so.build_suffix_array(corpus).astype(np.int32)
+        m = 8
+        pat = rng.integers(0, 4, size=(64, m)).astype(np.int32)
+        for i in range(0, 64, 3):
+            st = int(rng.integers(0, n - m))
+            pat[i] = corpus[st:st + m]
+        plen = rng.integers(-1, m + 3, size=64).astype(np.int64)
+        s, e = ops.search_interval(_dev(sa), _dev(corpus), _dev(pat),
+                                   _dev(plen))
+        es, ee = so.search_interval(sa, corpus, pat, plen)
+        np.testing.assert_array_equal(_host(s), es)
+        np.testing.assert_array_equal(_host(e), ee)
+        q = rng.integers(0, 4, size=(32, 10)).astype(np.int32)
+        qlen = rng.integers(-1, 14, size=32).astype(np.int64)
+        caps = np.array([16, 9, 5, 2, 1], dtype=np.int64)
+        got = ops.suffix_match_backoff(_dev(sa), _dev(corpus), _dev(q),
+                                       _dev(qlen), 12, _dev(caps))
+        exp = so.suffix_match_backoff(sa, corpus, q, qlen, 12, caps)
+        for g, x in zip(got, exp):
+            np.testing.assert_array_equal(_host(g), x)
+
+
+# ---------------------------------------------------------------------------
+# global index
+# ---------------------------------------------------------------------------
+def _gpu_drafter(**cfg):
+    from suffixgpu_b200 import SuffixGPUDrafter
+    return SuffixGPUDrafter(device=DEV, **cfg)
+
+
+@pytest.mark.parametrize("seed", [41, 42])
+def test_global_scenarios_match_goldens(golden_dir, seed):
+    z = np.load(os.path.join(golden_dir, f"global_{seed}.npz"))
+    sc = scenarios.global_scenario(seed)
+    got = scenarios.run_scenario(sc, _gpu_drafter, _dev, _host)
+    for key in ("draft", "num_valid", "new_counts", "final_tokens",
+                "active_len", "delta_len", "corpus", "sa"):
+        np.testing.assert_array_equal(got[key], z["out_" + key], key)
+
+
+@pytest.mark.parametrize("seed", [3, 4, 5])
+def test_global_scenarios_vs_oracle(seed):
+    sc = scenarios.global_scenario(seed, steps=12)
+    got = scenarios.run_scenario(sc, _gpu_drafter, _dev, _host)
+    exp = scenarios.run_scenario(sc, so.SuffixDrafter, lambda a: a.copy(),
+                                 lambda a: np.asarray(a).copy())
+    for key in ("draft", "num_valid", "new_counts", "final_tokens",
+                "active_len", "delta_len", "corpus", "sa"):
+        np.testing.assert_array_equal(got[key], exp[key], key)
+
+
+def _index_pair(**kw):
+    from suffixgpu_b200.global_index import GlobalIndex
+    return GlobalIndex(device=DEV, **kw), so.GlobalIndex(**kw)
+
+
+def test_delta_and_query_vs_oracle():
+    """Raw _delta_match_backoff / query outputs on a delta with repeats,
+    SEP boundaries and a long tail of candidates."""
+    rng = np.random.default_rng(11)
+    g, o = _index_pair(capacity=4096, delta_capacity=2000, k=6,
+                       max_occurrences=16, rebuild_threshold=100000)
+    docs = [rng.integers(0, 5, size=int(rng.integers(5, 120))).astype(
+        np.int32) for _ in range(20)]
+    g.append_documents([_dev(d) for d in docs])
+    o.append_documents(docs)
+    assert g.delta_len == o.delta_len
+    q = rng.integers(0, 5, size=(24, 9)).astype(np.int32)
+    qlen = rng.integers(-1, 11, size=24).astype(np.int64)
+    caps = np.array([9, 4, 2, 1, 0], dtype=np.int64)
+    got = g._delta_match_backoff(_dev(q), _dev(qlen), 9, _dev(caps))
+    exp = o._delta_match_backoff(q, qlen, 9, caps)
+    for a, b in zip(got, exp):
+        np.testing.assert_array_equal(_host(a), b)
+    for max_len in (3, 9):
+        got = g.query(_dev(q), _dev(qlen), max_len)
+        exp = o.query(q, qlen, max_len)
+        for a, b in zip(got, exp):
+            np.testing.assert_array_equal(_host(a), b)
+
+
+def test_rebuild_eviction_overflow_vs_oracle():
+    """Small capacities force eviction, delta overflow and whole-doc
+    snapshots; corpus, SA and queries stay identical."""
+    rng = np.random.default_rng(12)
+    g, o = _index_pair(capacity=300, delta_capacity=90, k=4,
+                       max_occurrences=8, rebuild_threshold=60)
+    for step in range(25):
+        docs = [rng.integers(0, 6, size=int(rng.integers(1, 40))).astype(
+            np.int32) for _ in range(int(rng.integers(1, 4)))]
+        g.append_documents([_dev(d) for d in docs])
+        o.append_documents(docs)
+        assert (g.active_len, g.delta_len) == (o.active_len, o.delta_len)
+        q = rng.integers(0, 6, size=(5, 6)).astype(np.int32)
+        qlen = np.full(5, 6, dtype=np.int64)
+        got = g.query(_dev(q), _dev(qlen), 6)
+        exp = o.query(q, qlen, 6)
+        for a, b in zip(got, exp):
+            np.testing.assert_array_equal(_host(a), b)
+    np.testing.assert_array_equal(_host(g.corpus), o.corpus)
+    np.testing.assert_array_equal(_host(g.sa), o.sa)
+
+
+def test_background_rebuild_swaps_at_poll():
+    """With a rebuild stream the build runs in the background; after it is
+    swapped in, the index equals the synchronous one."""
+    rng = np.random.default_rng(13)
+    from suffixgpu_b200.global_index import GlobalIndex
+    side = torch.cuda.Stream()
+    g = GlobalIndex(capacity=5000, delta_capacity=800, k=4,
+                    max_occurrences=8, rebuild_threshold=400, device=DEV,
+                    rebuild_stream=side)
+    o = so.GlobalIndex(capacity=5000, delta_capacity=800, k=4,
+                       max_occurrences=8, rebuild_threshold=400)
+    for _ in range(6):
+        docs = [rng.integers(0, 7, size=150).astype(np.int32)
+                for _ in range(2)]
+        g.append_documents([_dev(d) for d in docs])
+        g.wait_rebuild()
+        o.append_documents(docs)
+    assert g.rebuilds == o.rebuilds and g.rebuilds > 0
+    np.testing.assert_array_equal(_host(g.corpus), o.corpus)
+    np.testing.assert_array_equal(_host(g.sa), o.sa)
+
+
+class _NeverDoneEvent:
+    def query(self) -> bool:
+        return False
+
+
+def test_delta_overflow_with_rebuild_in_flight():
+    """Appends that overflow the delta while a rebuild is in flight drop
+    the oldest docs (global_index.py:110-133), checked against the
+    oracle with the same fake in-flight event."""
+    g, o = _index_pair(capacity=64, delta_capacity=18, k=4,
+                       max_occurrences=8, rebuild_threshold=100000)
+    for idx in (g, o):
+        idx.append_documents([np.full(6, 1, np.int32) if idx is o
+                              else _dev(np.full(6, 1, np.int32)),
+                              np.full(6, 2, np.int32) if idx is o
+                              else _dev(np.full(6, 2, np.int32))])
+        idx._rebuild_event = _NeverDoneEvent()
+        idx._pending = (idx.active_len, idx.active_doc_lens)
+    g.append_documents([_dev(np.full(10, 3, np.int32))])
+    o.append_documents([np.full(10, 3, np.int32)])
+    assert g.delta_len == o.delta_len <= 18
+    for pat in ([3, 3], [2, 2], [1, 1]):
+        q = np.array([pat], dtype=np.int32)
+        ql = np.array([2], dtype=np.int64)
+        got = g.query(_dev(q), _dev(ql), 8)
+        exp = o.query(q, ql, 8)
+        for a, b in zip(got, exp):
+            np.testing.assert_array_equal(_host(a), b)
