@@ -168,6 +168,21 @@ int sg_build_suffix_array(const int32_t* tokens, int64_t n, int32_t* sa_out,
                           void* workspace, size_t workspace_bytes,
                           int32_t* rounds_out, sg_stream_t stream);
 
+/* sg_build_suffix_array without any device allocation, for callers that
+ * cannot allocate (an engine that has reserved all GPU memory up front, a
+ * plugin host that only passes input and output buffers). No counterpart in
+ * the reference. The workspace is an 8 MiB static __device__ array inside
+ * this library (held by every GPU that loads it), so n is limited to about
+ * 231 thousand tokens; larger n returns SG_ERR_UNSUPPORTED without
+ * launching anything. The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress). All calls share the array: calls
+ * whose work overlaps on the GPU (other streams, other host threads) race
+ * and must be serialised by the caller. Synchronises `stream` like
+ * sg_build_suffix_array. */
+int sg_build_suffix_array_noalloc(const int32_t* tokens, int64_t n,
+                                  int32_t* sa_out, int32_t* rounds_out,
+                                  sg_stream_t stream);
+
 /* ---- suffix-array search (suffix_gpu/sa_search.py) ---------------------- */
 
 /* search_interval (sa_search.py:66-107, triton_kernels.py:284-302): SA

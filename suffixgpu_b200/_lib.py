@@ -76,6 +76,8 @@ _SIGS: dict[str, list] = {
                         c_void_p, c_void_p, c_void_p],
     "sg_build_suffix_array": [c_void_p, c_int64, c_void_p, c_void_p,
                               c_size_t, POINTER(c_int32), c_void_p],
+    "sg_build_suffix_array_noalloc": [c_void_p, c_int64, c_void_p,
+                                      POINTER(c_int32), c_void_p],
     "sg_sa_search": [c_void_p, c_void_p, c_int64, c_void_p, c_int32, c_int32,
                      c_void_p, c_void_p, c_void_p, c_void_p],
     "sg_suffix_match_backoff": [c_void_p, c_void_p, c_int64, c_void_p,

@@ -22,6 +22,8 @@
 // sm_100a).
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "sg_common.cuh"
 
 namespace sg {
@@ -530,4 +532,79 @@ extern "C" int sg_build_suffix_array(const int32_t* tokens, int64_t n,
   }
   if (rounds_out) *rounds_out = rounds;
   return check_launch();
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant
+// ---------------------------------------------------------------------------
+// Some callers cannot allocate device memory at all: a serving engine that
+// reserves all free GPU memory for its KV cache at start-up and forbids
+// later cudaMalloc calls, or a plugin host that owns every allocation and
+// only hands its plugins input and output buffers. For them the suffix-array
+// build can run on a scratch array compiled into this library. The array is
+// a file-scope __device__ variable: every GPU that loads the library holds
+// its kSaNoAllocScratchBytes until the process exits, whether or not the
+// entry point is used.
+namespace sg {
+
+constexpr size_t kSaNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB
+
+static __device__ __align__(256) unsigned char
+    g_sa_noalloc_scratch[kSaNoAllocScratchBytes];
+
+// Device address of the scratch array, looked up once per device. In host
+// code the array's name is only a host-side stand-in, so kernels must be
+// given the address cudaGetSymbolAddress returns for the current device.
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[64] = {nullptr};
+
+static int noalloc_scratch(void** out) {
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return SG_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_sa_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      set_cuda_error(e);
+      return SG_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return SG_OK;
+}
+
+// Largest n whose build workspace fits the scratch array.
+static int64_t noalloc_max_tokens() {
+  int64_t lo = 0, hi = static_cast<int64_t>(kSaNoAllocScratchBytes);
+  while (lo < hi) {
+    const int64_t mid = lo + (hi - lo + 1) / 2;
+    if (carve(nullptr, mid).bytes <= kSaNoAllocScratchBytes) {
+      lo = mid;
+    } else {
+      hi = mid - 1;
+    }
+  }
+  return lo;
+}
+
+}  // namespace sg
+
+extern "C" int sg_build_suffix_array_noalloc(const int32_t* tokens,
+                                             int64_t n, int32_t* sa_out,
+                                             int32_t* rounds_out,
+                                             sg_stream_t stream) {
+  if (n < 0) return SG_ERR_INVALID;
+  static const int64_t max_n = sg::noalloc_max_tokens();
+  if (n > max_n) return SG_ERR_UNSUPPORTED;  // input beyond the scratch size
+  void* scratch = nullptr;
+  // First call on a device: looks up the scratch address (no allocation).
+  const int rc = sg::noalloc_scratch(&scratch);
+  if (rc != SG_OK) return rc;
+  // The build zeroes the per-pass digit totals itself and writes every
+  // other scratch region before reading it, so the previous call's leftover
+  // contents need no clearing.
+  return sg_build_suffix_array(tokens, n, sa_out, scratch,
+                               sg::kSaNoAllocScratchBytes, rounds_out, stream);
 }
