@@ -56,6 +56,14 @@ def parse():
                     help="skip the end-to-end API leg (profiling runs)")
     ap.add_argument("--no-cpu", action="store_true",
                     help="skip the CPU baseline leg (profiling runs)")
+    ap.add_argument("--mode", default="draft", choices=["draft", "sa"],
+                    help="draft: config 2 (+ SA build line); sa: SA build "
+                         "only (config 4)")
+    ap.add_argument("--sa-log2n", type=int, default=24,
+                    help="SA build size (config 4: 2^24 tokens)")
+    ap.add_argument("--sa-reps", type=int, default=5)
+    ap.add_argument("--no-sa", action="store_true",
+                    help="skip the SA build measurement in draft mode")
     return ap.parse_args()
 
 
@@ -293,11 +301,62 @@ def run_ours(args):
         }
         res["cpu_baseline"] = None if (args.no_cpu or world > 1) \
             else cpu_baseline(args, data)
+        if not args.no_sa:
+            res["sa_build"] = run_sa(args, dev)
     if world > 1:
         dist.barrier()
         del full, part
         dist.destroy_process_group()
     return res
+
+
+def sa_alg_bytes(n: int, rounds: int) -> float:
+    """Algorithmic bytes of one SA build: read the tokens and write the SA
+    (8n) plus, per doubling round, gathering two ranks, writing a rank and
+    LSD 8-bit passes over (key, u32 index) records with a 2*ceil(log2(n+1))
+    bit key: h * n * (12 + 24 * ceil(2 * ceil(log2(n + 1)) / 8))."""
+    import math
+    kb = 2 * math.ceil(math.log2(n + 1))
+    return 8 * n + rounds * n * (12 + 24 * math.ceil(kb / 8))
+
+
+def run_sa(args, dev) -> dict:
+    """suffix array of 2^24 tokens (50% i.i.d. Zipf,
+    50% copies of earlier spans). Times whole builds with CUDA events; the
+    build synchronises once per doubling round, so the time includes those
+    host round trips."""
+    import torch
+    from suffixgpu_b200 import ops
+    from suffixgpu_b200 import workloads as wl
+    n = 1 << args.sa_log2n
+    tok = torch.from_numpy(wl.config4(n=n, n_queries=1)["tokens"]).to(dev)
+    out = torch.empty(n, dtype=torch.int32, device=dev)
+    rounds = ops.build_suffix_array_into(tok, out)  # warm-up (+ workspace)
+    ops.build_suffix_array_into(tok, out)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(max(1, args.sa_reps)):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        rounds = ops.build_suffix_array_into(tok, out)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = float(statistics.median(times))
+    alg = sa_alg_bytes(n, rounds)
+    peaks = _peaks()
+    achieved = alg / (ms * 1e-3) / 1e9
+    return {"metric": "SA build Mtok/s", "value": n / (ms * 1e-3) / 1e6,
+            "unit": "Mtok/s", "n_tokens": n, "ms_per_build": ms,
+            "doubling_rounds": rounds, "reps": len(times),
+            "workload": "config4: 2^24 tokens, 50% Zipf(1.1) / 50% copies "
+                        "U[32,1024], vocab 128256",
+            "roofline": {"bound": "hbm", "achieved": achieved,
+                         "peak": peaks["hbm_gbs"],
+                         "peak_source": peaks["source"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"],
+                         "alg_bytes_per_build": alg}}
 
 
 def run_e2e(args, drafter, reps, data, dev, world):
@@ -442,6 +501,11 @@ def main():
     args = parse()
     if args.impl == "reference":
         res = run_reference(args)
+    elif args.mode == "sa":
+        import torch
+        dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        torch.cuda.set_device(dev)
+        res = run_sa(args, dev)
     else:
         res = run_ours(args)
     if res is not None:
