@@ -13,13 +13,15 @@
 //      shared copy and the HBM buffer (update_state semantics).
 //   2. match_back for every end position i < q. Each warp owns a contiguous
 //      segment of positions and appends the nonzero ones, in position order,
-//      to its own hit list (ballot prefix sums, no block-wide scan); a
-//      (P+1)-bin histogram of the values is kept with warp-aggregated
-//      atomics. The reference's topk over [B,S] becomes a count over the
-//      histogram: the t-th largest value is the largest L with
+//      to its own hit list (one packed prefix sum per 256 words, no
+//      block-wide scan), then turns its histogram of the values into
+//      #{mb >= L} per length. The reference's topk over [B,S] becomes a
+//      count over these: the t-th largest value is the largest L with
 //      #{mb >= L} >= t.
-//   3. One warp per candidate walks the hit lists in order (32 entries per
-//      ballot) to collect its earliest R occurrences, then expands its
+//   3. The earliest R occurrences of each candidate: with few hits the
+//      candidate's warp walks the lists in order (32 entries per ballot);
+//      otherwise every warp writes its qualifying hits at the offset the
+//      per-warp counts give. One warp per candidate then expands its
 //      continuation chain (sg_vote.cuh) reading continuations straight from
 //      the shared row, stopping at the candidate's spec cap.
 //   4. argmax(score + f32(cand) * 1e-6) and the masked draft write.
@@ -42,8 +44,8 @@ constexpr int kWalkHits = 256;  // rows with at most this many hits: walk
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 
 struct LocalLayout {
-  size_t off_tok, off_hits, off_pat, off_hist, off_cand, off_score, off_emit;
-  size_t off_chain, off_wlen, off_wcnt, off_occ, off_warp, warp_bytes;
+  size_t off_tok, off_hits, off_pat, off_whist, off_cge, off_cand, off_score;
+  size_t off_emit, off_chain, off_wlen, off_occ, off_warp, warp_bytes;
   size_t total;
   int H;
   __host__ __device__ LocalLayout(int S, int P, int C, int R, int K) {
@@ -54,13 +56,15 @@ struct LocalLayout {
     // per-warp hit lists: segments are rounded up to 128 positions each
     off_hits = o;  o = align16(o + 4 * s4 + 4 * 128 * kLocalWarps);
     off_pat = o;   o = align16(o + 4 * static_cast<size_t>(P));
-    off_hist = o;  o = align16(o + 4 * static_cast<size_t>(P + 2));
+    // per warp: #{hits with mb >= L} for L = 0..P+1 (a histogram until the
+    // warp's suffix sum turns it into counts)
+    off_whist = o; o = align16(o + 4 * static_cast<size_t>(P + 2) * kLocalWarps);
+    off_cge = o;   o = align16(o + 4 * static_cast<size_t>(P + 2));
     off_cand = o;  o = align16(o + 4 * kMaxCand);
     off_score = o; o = align16(o + 4 * kMaxCand);
     off_emit = o;  o = align16(o + 4 * kMaxCand);
     off_chain = o; o = align16(o + 4 * static_cast<size_t>(C) * K);
-    off_wlen = o;  o = align16(o + 8 * kLocalWarps);  // lengths + max mb
-    off_wcnt = o;  o = align16(o + 4 * static_cast<size_t>(kLocalWarps) * kMaxCand);
+    off_wlen = o;  o = align16(o + 4 * kLocalWarps);
     off_occ = o;   o = align16(o + 4 * static_cast<size_t>(C) * R);
     warp_bytes = align16(4 * static_cast<size_t>(R > 64 ? R : 64) +
                          8 * static_cast<size_t>(H));
@@ -85,32 +89,28 @@ __device__ __forceinline__ long long spec_cap(const sg_draft_params& p,
   return c > 0 ? c : 0;
 }
 
-// Candidate lengths for support thresholds 2^0..2^(C-1), from the
-// histogram of match_back values (local_matcher.py:134-157): cand_t is the
-// t-th largest mb, i.e. the largest L with #{mb >= L} >= t (0 if none),
-// zeroed below min_match_len and when equal to the previous candidate.
+// Candidate lengths for support thresholds 2^0..2^(C-1)
+// (local_matcher.py:134-157): cand_t is the t-th largest match_back value,
+// i.e. the largest L with #{mb >= L} >= t (0 if none), zeroed below
+// min_match_len and when equal to the previous candidate. ge[w * (P + 2) +
+// L] holds warp w's #{mb >= L}; the block totals go to cge when given.
 // Executed by a full warp; lane c < C returns candidate c.
-__device__ __forceinline__ int warp_candidates(const int* hist, int P, int C,
-                                               int min_match) {
+__device__ __forceinline__ int warp_candidates(const int* ge, int P, int C,
+                                               int min_match, int* cge) {
   const int lane = lane_id();
+  const int stride = P + 2;
   int cand = 0;
-  int carry = 0;  // #{mb > top length of the current chunk}
-  const int nchunk = (P + 31) / 32;
-  for (int ch = nchunk - 1; ch >= 0; --ch) {
-    const int L = ch * 32 + 1 + lane;  // lengths 32ch+1 .. 32ch+32
-    int v = L <= P ? hist[L] : 0;
-    // suffix sum within the chunk: sum over lanes >= lane
+  for (int L0 = 1; L0 <= P; L0 += 32) {
+    const int L = L0 + lane;
+    int v = 0;
+    if (L <= P) {
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int u = __shfl_down_sync(SG_FULL_MASK, v, o);
-      if (lane + o < 32) v += u;
+      for (int w = 0; w < kLocalWarps; ++w) v += ge[w * stride + L];
+      if (cge) cge[L] = v;
     }
-    const int cnt_ge = v + carry;
-    carry += __shfl_sync(SG_FULL_MASK, v, 0);
     // cand_c = #{L : cnt_ge[L] >= 2^c}: cnt_ge is non-increasing in L
     for (int c = 0; c < C; ++c) {
-      const unsigned m =
-          __ballot_sync(SG_FULL_MASK, L <= P && cnt_ge >= (1ll << c));
+      const unsigned m = __ballot_sync(SG_FULL_MASK, L <= P && v >= (1 << c));
       if (lane == c) cand += __popc(m);
     }
   }
@@ -132,14 +132,13 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
   int* tok_s = reinterpret_cast<int*>(smem + L.off_tok);
   int* hits = reinterpret_cast<int*>(smem + L.off_hits);
   int* pat = reinterpret_cast<int*>(smem + L.off_pat);
-  int* hist = reinterpret_cast<int*>(smem + L.off_hist);
+  int* whist = reinterpret_cast<int*>(smem + L.off_whist);  // [warps][P+2]
+  int* cge = reinterpret_cast<int*>(smem + L.off_cge);      // [P+2]
   float* score_s = reinterpret_cast<float*>(smem + L.off_score);
   int* emit_s = reinterpret_cast<int*>(smem + L.off_emit);
   int* cand_s = reinterpret_cast<int*>(smem + L.off_cand);
   int* chain_s = reinterpret_cast<int*>(smem + L.off_chain);
   int* wlen = reinterpret_cast<int*>(smem + L.off_wlen);
-  int* wmax = wlen + kLocalWarps;
-  int* wcnt = reinterpret_cast<int*>(smem + L.off_wcnt);  // [warps][cands]
   int* occ_s = reinterpret_cast<int*>(smem + L.off_occ);  // [cands][R]
 
   __shared__ long long s_q, s_base, s_cnt;
@@ -182,12 +181,15 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
     } else {
       m = a.in.mask ? (a.in.mask[b] != 0) : 1;
     }
+    const long long nl = q < 0 ? 0 : (q < S ? q : S);
+    const int nload = m ? static_cast<int>(nl) : 0;
+    int nal = nload & ~3;
+    if ((reinterpret_cast<uintptr_t>(row) & 15) != 0) nal = 0;
+    // a ragged tail of up to 32 tokens is read here, beside the bulk copy
+    // (disjoint shared-memory ranges)
+    if (nload - nal <= 32 && nal + lane < nload) tok_s[nal + lane] = row[nal + lane];
     if (lane == 0) {
       if (srow) a.out.new_counts[b] = static_cast<int32_t>(q);
-      const long long nl = q < 0 ? 0 : (q < S ? q : S);
-      const int nload = m ? static_cast<int>(nl) : 0;
-      int nal = nload & ~3;
-      if ((reinterpret_cast<uintptr_t>(row) & 15) != 0) nal = 0;
       s_q = q; s_base = base; s_cnt = cnt; s_mask = m;
       s_nload = nload; s_nal = nal;
       if (nal > 0) {
@@ -205,15 +207,17 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
   } else {
     // other warps: empty their vote tables while the loads are in flight
     vote_table_clear(vs);
-    for (int i = t - 32; i < P + 2; i += kLocalThreads - 32) hist[i] = 0;
+    for (int i = t - 32; i < (P + 2) * kLocalWarps; i += kLocalThreads - 32)
+      whist[i] = 0;
   }
   __syncthreads();
   const long long q = s_q;
   // q clamped into int range: positions are < S < 2^23
   const int q32 = q > INT32_MAX ? INT32_MAX : (q < INT32_MIN ? INT32_MIN : static_cast<int>(q));
   const int mask = s_mask, nload = s_nload, nal = s_nal;
-  // ragged tail (or the whole row when it is not 16-byte aligned)
-  for (int i = nal + t; i < nload; i += kLocalThreads) tok_s[i] = row[i];
+  // the whole row when it is not 16-byte aligned
+  if (nload - nal > 32)
+    for (int i = nal + t; i < nload; i += kLocalThreads) tok_s[i] = row[i];
   bool timed_out = false;
   if (nal > 0 && !mbar_wait(bar, 0)) {
     // A bulk copy of resident memory always lands; should the bound ever
@@ -270,8 +274,15 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
   }
 
   // ---- 2. match_back: ordered hit lists per warp segment -----------------
+  // Each warp owns a contiguous segment of 1024-token chunks. In a chunk,
+  // lane l examines the 32 tokens [32 l, 32 l + 32) as one bit mask; its 8
+  // vector loads go in a lane-rotated order, so each load instruction of the
+  // warp is free of bank conflicts. One prefix sum of the per-lane hit
+  // counts then places the positions in order.
   const int nw = (nload + 3) >> 2;  // 4-token words
-  const int seg = ((nw + kLocalWarps - 1) / kLocalWarps + 31) & ~31;
+  const int seg = ((nw + kLocalWarps - 1) / kLocalWarps + 255) & ~255;
+  const int hstride = P + 2;
+  int* my_ge = whist + warp * hstride;
   int* my_hits;
   int nh = 0;
   {
@@ -280,39 +291,56 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
     my_hits = hits + static_cast<size_t>(w_begin) * 4;  // 4*seg slots
     const int4* tok4 = reinterpret_cast<const int4*>(tok_s);
     const int pt0 = pat[0];
-    // 2a. positions i with tok[i-1] == pat[0], in order
-    int carry = (w_begin > 0 && w_begin < nw) ? tok_s[4 * w_begin - 1] : -1;
-    for (int w0 = w_begin; w0 < w_end; w0 += 32) {
-      const int w = w0 + lane;
-      const int4 cur = w < w_end ? tok4[w] : make_int4(0, 0, 0, 0);
-      int before0 = __shfl_up_sync(SG_FULL_MASK, cur.w, 1);
-      if (lane == 0) before0 = carry;
-      carry = __shfl_sync(SG_FULL_MASK, cur.w, 31);
-      unsigned hm = 0;
-      if (w < w_end) {
-        const int rem = nload - 4 * w;
-        const unsigned vm = rem >= 4 ? 0xFu : ((1u << rem) - 1u);
-        hm = ((before0 == pt0) | ((cur.x == pt0) << 1) |
-              ((cur.y == pt0) << 2) | ((cur.z == pt0) << 3)) & vm;
-      }
-      if (__ballot_sync(SG_FULL_MASK, hm != 0) == 0) continue;
-      const int nz = __popc(hm);
-      const unsigned b0 = __ballot_sync(SG_FULL_MASK, nz & 1);
-      const unsigned b1 = __ballot_sync(SG_FULL_MASK, nz & 2);
-      const unsigned b2 = __ballot_sync(SG_FULL_MASK, nz & 4);
-      int pos = nh + __popc(b0 & lt_mask) + 2 * __popc(b1 & lt_mask) +
-                4 * __popc(b2 & lt_mask);
+    // 2a. positions i with tok[i-1] == pat[0], in order; positions before
+    // the buffer start read -1
+    uint32_t carry = 0;  // token before the chunk == pat[0]
+    if (w_begin < nw)
+      carry = (w_begin > 0 ? tok_s[4 * w_begin - 1] : -1) == pt0;
+    for (int c0 = w_begin; c0 < w_end; c0 += 256) {
+      const int wl = c0 + 8 * lane;  // this lane's first word
+      uint32_t eq = 0;               // bit q: token 4 wl + q == pat[0]
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (hm & (1u << k)) my_hits[pos++] = 4 * w + k;
-      nh += __popc(b0) + 2 * __popc(b1) + 4 * __popc(b2);
+      for (int k = 0; k < 8; ++k) {
+        const int j = (k + lane) & 7;
+        if (wl + j < w_end) {
+          const int4 v = tok4[wl + j];
+          const uint32_t bits = static_cast<uint32_t>(v.x == pt0) |
+                                (static_cast<uint32_t>(v.y == pt0) << 1) |
+                                (static_cast<uint32_t>(v.z == pt0) << 2) |
+                                (static_cast<uint32_t>(v.w == pt0) << 3);
+          eq |= bits << (4 * j);
+        }
+      }
+      // end position 4 wl + p is a hit iff token 4 wl + p - 1 matches: bit
+      // p - 1 of eq, or bit 31 of the previous lane's mask for p = 0
+      const uint32_t up = __shfl_up_sync(SG_FULL_MASK, eq, 1);
+      uint32_t hm = (eq << 1) | (lane == 0 ? carry : (up >> 31));
+      carry = __shfl_sync(SG_FULL_MASK, eq, 31) >> 31;
+      const int p0 = 4 * wl;
+      const int nvalid = nload - p0;  // positions >= nload are not ends
+      if (nvalid < 32) hm &= nvalid <= 0 ? 0u : ((1u << nvalid) - 1u);
+      if (__ballot_sync(SG_FULL_MASK, hm != 0) == 0) continue;
+      const int c = __popc(hm);
+      int inc = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int x = __shfl_up_sync(SG_FULL_MASK, inc, o);
+        if (lane >= o) inc += x;
+      }
+      int pos = nh + inc - c;
+      while (hm) {
+        const int bit = __ffs(hm) - 1;
+        hm &= hm - 1;
+        my_hits[pos++] = p0 + bit;
+      }
+      nh += __shfl_sync(SG_FULL_MASK, inc, 31);
     }
     __syncwarp();
     // 2b. extend every hit; consecutive lanes take consecutive hits
     const int pt1 = P > 1 ? pat[1] : INT32_MIN;
     const int pt2 = P > 2 ? pat[2] : INT32_MIN;
     const int pt3 = P > 3 ? pat[3] : INT32_MIN;
-    int h1 = 0, h2 = 0, h3 = 0, h4 = 0, mmax = 0;
+    int h1 = 0, h2 = 0, h3 = 0, h4 = 0;
     for (int i = lane; i < nh; i += 32) {
       const int e = my_hits[i];
       const int t1 = e >= 2 ? tok_s[e - 2] : -1;
@@ -339,80 +367,74 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
       h2 += m == 2;
       h3 += m == 3;
       h4 += m == 4;
-      if (m > 4) atomicAdd(&hist[m], 1);
-      mmax = max(mmax, m);
+      if (m > 4) atomicAdd(&my_ge[m], 1);
       my_hits[i] = (e << 8) | m;
     }
     h1 = warp_sum(h1);
     h2 = warp_sum(h2);
     h3 = warp_sum(h3);
     h4 = warp_sum(h4);
-    mmax = __reduce_max_sync(SG_FULL_MASK, mmax);
+    __syncwarp();  // this warp's atomics on my_ge have landed
+    // histogram -> #{hits with mb >= L}, suffix sums from the top chunk
+    int above = 0;  // #{hits with mb above this chunk of lengths}
+    for (int L0 = ((P - 1) & ~31) + 1; L0 >= 1; L0 -= 32) {
+      const int Lx = L0 + lane;
+      int v = Lx <= P ? my_ge[Lx] : 0;
+      v += Lx == 1 ? h1 : Lx == 2 ? h2 : Lx == 3 ? h3 : Lx == 4 ? h4 : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_down_sync(SG_FULL_MASK, v, o);
+        if (lane + o < 32) v += u;
+      }
+      v += above;
+      above = __shfl_sync(SG_FULL_MASK, v, 0);
+      if (Lx <= P) my_ge[Lx] = v;
+    }
     if (lane == 0) {
+      my_ge[P + 1] = 0;
       wlen[warp] = nh;
-      wmax[warp] = mmax;
-      if (h1) atomicAdd(&hist[1], h1);
-      if (h2) atomicAdd(&hist[2], h2);
-      if (h3) atomicAdd(&hist[3], h3);
-      if (h4) atomicAdd(&hist[4], h4);
     }
   }
   __syncthreads();
 
   // ---- 3. candidates and their earliest R occurrences -------------------
-  const int cand_lane = warp_candidates(hist, P, C, p.min_match_len);
+  const int cand_lane =
+      warp_candidates(whist, P, C, p.min_match_len, warp == 0 ? cge : nullptr);
   if (warp == 0 && lane < C) cand_s[lane] = cand_lane;
   int total_hits = 0;
 #pragma unroll
   for (int w = 0; w < kLocalWarps; ++w) total_hits += wlen[w];
   // Few hits: each candidate's warp walks every list itself (no extra
-  // barriers). Many hits: every warp counts its own list per candidate,
-  // then writes its share at the prefix offset.
+  // barrier). Many hits: every warp writes its qualifying hits at the
+  // offset given by the per-warp counts of the warps before it.
   const bool walk = total_hits <= kWalkHits;
   if (!walk) {
-    const int my_max = wmax[warp];
-    int mycnt = 0;  // lane c: hits in this warp's list with mb >= cand_c
-    {
-      int cr[NC], k[NC];
-#pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        cr[c] = c < C ? __shfl_sync(SG_FULL_MASK, cand_lane, c) : 0;
-        if (cr[c] > my_max) cr[c] = 0;  // no entry of this list qualifies
-        k[c] = 0;
-      }
-      for (int i = lane; i < nh; i += 32) {
-        const int m = my_hits[i] & 0xff;
-#pragma unroll
-        for (int c = 0; c < NC; ++c) k[c] += (cr[c] > 0 && m >= cr[c]);
-      }
-#pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        if (c < C) {
-          const int tot = __reduce_add_sync(SG_FULL_MASK, k[c]);
-          if (lane == c) mycnt = tot;
-        }
-      }
-    }
-    if (lane < C) wcnt[warp * kMaxCand + lane] = mycnt;
-    __syncthreads();
-    // earliest R end positions per candidate, written at this warp's
-    // offset (local_matcher.py:160-184)
+    // earliest R end positions per candidate (local_matcher.py:160-184)
     for (int c = 0; c < C; ++c) {
       const int cand = __shfl_sync(SG_FULL_MASK, cand_lane, c);
-      const int k = __shfl_sync(SG_FULL_MASK, mycnt, c);
-      if (cand == 0 || k == 0) continue;
+      if (cand == 0) continue;
+      const int k = my_ge[cand];
+      if (k == 0) continue;
       int off = 0;
-      for (int w = 0; w < warp; ++w) off += wcnt[w * kMaxCand + c];
+      for (int w = 0; w < warp; ++w) off += whist[w * hstride + cand];
       if (off >= R) continue;
-      int* oc = occ_s + c * R;
-      for (int i0 = 0; i0 < nh && off < R; i0 += 32) {
-        const int i = i0 + lane;
-        const int e = i < nh ? my_hits[i] : 0;
-        const bool hit = i < nh && (e & 0xff) >= cand;
-        const unsigned bal = __ballot_sync(SG_FULL_MASK, hit);
-        const int r = off + __popc(bal & lt_mask);
-        if (hit && r < R) oc[r] = e >> 8;
-        off += __popc(bal);
+      int* oc = occ_s + c * R + off;
+      const int room = R - off;
+      if (k == nh) {
+        // every hit of this list qualifies: a straight copy
+        const int lim = nh < room ? nh : room;
+        for (int i = lane; i < lim; i += 32) oc[i] = my_hits[i] >> 8;
+      } else {
+        int got = 0;
+        for (int i0 = 0; i0 < nh && got < k && got < room; i0 += 32) {
+          const int i = i0 + lane;
+          const int e = i < nh ? my_hits[i] : 0;
+          const bool hit = i < nh && (e & 0xff) >= cand;
+          const unsigned bal = __ballot_sync(SG_FULL_MASK, hit);
+          const int r = got + __popc(bal & lt_mask);
+          if (hit && r < room) oc[r] = e >> 8;
+          got += __popc(bal);
+        }
       }
     }
     __syncthreads();
@@ -436,10 +458,12 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
       // earliest R end positions with mb >= cand, in position order
       int* ocw = occ_s + c * R;
       for (int w = 0; w < kLocalWarps && n < R; ++w) {
-        if (wmax[w] < cand) continue;
+        const int kw = whist[w * hstride + cand];  // qualifying entries
+        if (kw == 0) continue;
         const int* lst = hits + static_cast<size_t>(w) * seg * 4;
         const int len = wlen[w];
-        for (int i0 = 0; i0 < len && n < R; i0 += 32) {
+        const int stop = n + kw;
+        for (int i0 = 0; i0 < len && n < stop && n < R; i0 += 32) {
           const int e = i0 + lane < len ? lst[i0 + lane] : 0;
           const bool hit = (e & 0xff) >= cand;
           const unsigned bal = __ballot_sync(SG_FULL_MASK, hit);
@@ -450,7 +474,7 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
       }
       __syncwarp();
     } else {
-      for (int w = 0; w < kLocalWarps; ++w) n += wcnt[w * kMaxCand + c];
+      for (int w = 0; w < kLocalWarps; ++w) n += whist[w * hstride + cand];
     }
     if (n > R) n = R;
     // continuation tokens (local_matcher.py:186-195): tok[e + d] if e+d < q
@@ -503,8 +527,7 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
         // occurrence count of the chosen candidate: min(#{mb >= cand}, R)
         int occ = 0;
         if (best >= 0 && cand_s[best] > 0) {
-          int ge = 0;
-          for (int l = cand_s[best]; l <= P; ++l) ge += hist[l];
+          const int ge = cge[cand_s[best]];
           occ = ge < R ? ge : R;
         }
         a.out.best_occ[b] = occ;

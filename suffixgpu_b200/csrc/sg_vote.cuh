@@ -16,9 +16,11 @@
 // slot and votes:
 //   * <= 32 survivors (one per lane): each lane counts its token among the
 //     32 in a shared buffer (8 vector loads), then two warp reductions;
-//   * more: a per-warp open-addressing table in shared memory, one CAS
-//     insert + one atomic add per token, all of a lane's in flight together;
-//     every lane then empties the slots it used.
+//   * more: the first voting token is counted with ballots and wins on a
+//     strict majority; otherwise the other tokens go through a per-warp
+//     open-addressing table in shared memory, one CAS insert + one atomic
+//     add per token, all of a lane's in flight together; every lane then
+//     empties the slots it used.
 // The winner's non-matching occurrences drop their alive bit; once <= 32
 // remain they are compacted to one per lane. While all survivors agree, up
 // to 8 depths are committed at once from a shared lookahead.
@@ -152,6 +154,54 @@ __device__ __forceinline__ void vote_hash(const int (&v)[RJ], int nslots,
   __syncwarp();
 }
 
+// Plurality vote over RJ slots per lane. The first voting token (the
+// leader) is counted with ballots; a strict majority wins outright. Only
+// otherwise do the remaining tokens go through the hash table, with the
+// leader's tokens left out: copies make one continuation dominate, and
+// inserting 32 equal keys serialises the table's atomics on one slot.
+template <int RJ>
+__device__ __forceinline__ void vote_multi(const int (&v)[RJ], int nslots,
+                                           const VoteScratch& vs,
+                                           int& best_cnt, int& best_tok,
+                                           int& n_act) {
+  int ref = -1, na = 0;
+#pragma unroll
+  for (int j = 0; j < RJ; ++j) {
+    if (j < nslots) {
+      const unsigned bal = __ballot_sync(SG_FULL_MASK, v[j] != -1);
+      na += __popc(bal);
+      if (ref == -1 && bal) ref = __shfl_sync(SG_FULL_MASK, v[j], __ffs(bal) - 1);
+    }
+  }
+  n_act = na;
+  if (na == 0) {
+    best_cnt = 0;
+    best_tok = INT32_MAX;
+    return;
+  }
+  int cr = 0;
+#pragma unroll
+  for (int j = 0; j < RJ; ++j)
+    if (j < nslots) cr += __popc(__ballot_sync(SG_FULL_MASK, v[j] == ref));
+  if (2 * cr > na) {
+    best_cnt = cr;
+    best_tok = ref;
+    return;
+  }
+  int w[RJ];
+#pragma unroll
+  for (int j = 0; j < RJ; ++j) w[j] = v[j] == ref ? -1 : v[j];
+  int hc, ht, hn;
+  vote_hash<RJ>(w, nslots, vs, hc, ht, hn);
+  if (hc > cr || (hc == cr && ht < ref)) {
+    best_cnt = hc;
+    best_tok = ht;
+  } else {
+    best_cnt = cr;
+    best_tok = ref;
+  }
+}
+
 // Expand one candidate with the calling (full) warp.
 //   key_of(i): key of the i-th occurrence, i < n_occ (read once)
 //   cont(key, d): continuation token of that occurrence at depth d (-1 =
@@ -194,33 +244,69 @@ __device__ ExpandResult warp_expand(KeyFn key_of, ContFn cont, int n_occ,
   int nv = 0;
   int written = 0;  // depths [0, written) of chain_out are final
   int first = 0;    // lowest alive lane when nslots == 1
+  bool unanimous = false;  // the last multi-slot vote had every survivor agree
   for (int d = 0; d < depth_end && n > 0; ++d) {
-    if (nslots == 1) {
+    if (nslots == 1 || unanimous) {
       // Unanimous lookahead: while every survivor has the same token, the
       // vote is that token with count = active = survivors, so the depths
-      // can be committed without voting (same fp32 steps).
-      const bool alive = amask & 1u;
+      // can be committed without voting (same fp32 steps). With one slot
+      // per lane it is tried at every depth; with more, only after a
+      // unanimous vote, and the first survivor (lowest slot, then lowest
+      // lane) publishes its tokens before the others compare.
       const int ahead = min(8, depth_end - d);
-      int tk[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        tk[u] = (u < ahead && alive) ? cont(e[0], d + u) : -1;
-      if (lane == first) {
-#pragma unroll
-        for (int u = 0; u < 8; ++u) ref[u] = tk[u];
-      }
-      __syncwarp();
+      int r[8];
       int agree = ahead;
+      if (nslots == 1) {
+        const bool alive = amask & 1u;
+        int tk[8];
 #pragma unroll
-      for (int u = 7; u >= 0; --u) {
-        const int r = ref[u];
-        if (u < ahead && (r == -1 || (alive && tk[u] != r))) agree = u;
+        for (int u = 0; u < 8; ++u)
+          tk[u] = (u < ahead && alive) ? cont(e[0], d + u) : -1;
+        if (lane == first) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) ref[u] = tk[u];
+        }
+        __syncwarp();
+#pragma unroll
+        for (int u = 7; u >= 0; --u) {
+          r[u] = ref[u];
+          if (u < ahead && (r[u] == -1 || (alive && tk[u] != r[u]))) agree = u;
+        }
+      } else {
+        int l0 = -1, ej = 0;
+#pragma unroll
+        for (int j = 0; j < RJ; ++j) {
+          if (j < nslots) {
+            const unsigned bal = __ballot_sync(SG_FULL_MASK, (amask >> j) & 1u);
+            if (l0 < 0 && bal) {
+              l0 = __ffs(bal) - 1;
+              ej = e[j];
+            }
+          }
+        }
+        if (lane == l0) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) ref[u] = u < ahead ? cont(ej, d + u) : -1;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int u = 7; u >= 0; --u) {
+          r[u] = ref[u];
+          if (u < ahead && r[u] == -1) agree = u;
+        }
+#pragma unroll
+        for (int j = 0; j < RJ; ++j) {
+          if (j < nslots && ((amask >> j) & 1u)) {
+            int aj = agree;
+#pragma unroll
+            for (int u = 7; u >= 0; --u)
+              if (u < agree && cont(e[j], d + u) != r[u]) aj = u;
+            agree = aj < agree ? aj : agree;
+          }
+        }
       }
       const int run = __reduce_min_sync(SG_FULL_MASK, agree);
       if (run > 0) {
-        int tok_u[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) tok_u[u] = ref[u];
         const float ratio = unit_alpha
             ? 1.0f
             : __fdiv_rn(static_cast<float>(n),
@@ -231,7 +317,7 @@ __device__ ExpandResult warp_expand(KeyFn key_of, ContFn cont, int n_occ,
           if (u < run && !stop) {
             prob = __fmul_rn(prob, ratio);
             const bool valid = prob >= min_prob;
-            if (lane == 0) chain_out[d + u] = valid ? tok_u[u] : -1;
+            if (lane == 0) chain_out[d + u] = valid ? r[u] : -1;
             written = d + u + 1;
             if (!valid) {
               stop = true;
@@ -244,6 +330,7 @@ __device__ ExpandResult warp_expand(KeyFn key_of, ContFn cont, int n_occ,
         }
         __syncwarp();
         if (stop) break;
+        if (run < ahead) unanimous = false;  // depth d + run disagrees
         d += run - 1;  // the loop's ++d moves to the first undecided depth
         continue;
       }
@@ -259,7 +346,8 @@ __device__ ExpandResult warp_expand(KeyFn key_of, ContFn cont, int n_occ,
     if (nslots == 1) {
       vote_small(v[0], vs.act, best_cnt, best_tok, n_act);
     } else {
-      vote_hash<RJ>(v, nslots, vs, best_cnt, best_tok, n_act);
+      vote_multi<RJ>(v, nslots, vs, best_cnt, best_tok, n_act);
+      unanimous = best_cnt == n && n_act == n;
     }
     // fp32 chain probability, correctly rounded, no contraction; a
     // unanimous vote with alpha 0 divides a count by itself: exactly 1
