@@ -56,14 +56,21 @@ def parse():
                     help="skip the end-to-end API leg (profiling runs)")
     ap.add_argument("--no-cpu", action="store_true",
                     help="skip the CPU baseline leg (profiling runs)")
-    ap.add_argument("--mode", default="draft", choices=["draft", "sa"],
-                    help="draft: config 2 (+ SA build line); sa: SA build "
-                         "only (config 4)")
+    ap.add_argument("--mode", default="draft",
+                    choices=["draft", "sa", "global"],
+                    help="draft: config 2 (+ SA build, SA query and "
+                         "global-path lines); sa: SA build + queries only "
+                         "(config 4); global: config 3 only")
     ap.add_argument("--sa-log2n", type=int, default=24,
                     help="SA build size (config 4: 2^24 tokens)")
     ap.add_argument("--sa-reps", type=int, default=5)
     ap.add_argument("--no-sa", action="store_true",
                     help="skip the SA build measurement in draft mode")
+    ap.add_argument("--no-global", action="store_true",
+                    help="skip the config 3 measurement in draft mode")
+    ap.add_argument("--global-steps", type=int, default=60,
+                    help="timed decode steps of config 3")
+    ap.add_argument("--global-warmup", type=int, default=8)
     return ap.parse_args()
 
 
@@ -303,6 +310,8 @@ def run_ours(args):
             else cpu_baseline(args, data)
         if not args.no_sa:
             res["sa_build"] = run_sa(args, dev)
+        if not args.no_global:
+            res["global"] = run_global(args, dev)
     if world > 1:
         dist.barrier()
         del full, part
@@ -347,6 +356,7 @@ def run_sa(args, dev) -> dict:
     alg = sa_alg_bytes(n, rounds)
     peaks = _peaks()
     achieved = alg / (ms * 1e-3) / 1e9
+    queries = run_queries(args, tok, out, dev, peaks)
     return {"metric": "SA build Mtok/s", "value": n / (ms * 1e-3) / 1e6,
             "unit": "Mtok/s", "n_tokens": n, "ms_per_build": ms,
             "doubling_rounds": rounds, "reps": len(times),
@@ -356,7 +366,154 @@ def run_sa(args, dev) -> dict:
                          "peak": peaks["hbm_gbs"],
                          "peak_source": peaks["source"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"],
-                         "alg_bytes_per_build": alg}}
+                         "alg_bytes_per_build": alg},
+            "sa_search": queries}
+
+
+def run_queries(args, tok, sa, dev, peaks) -> dict:
+    """BASELINE config 4 queries: 1000 corpus substrings per capped length
+    (32, 16, 8, 4, 2) against the built SA, all 5000 in one search_interval
+    launch (rows padded to width 32, pattern length per row). Every pattern
+    occurs in the corpus, so every interval must be non-empty: a
+    size-independent check of the full-size search. Algorithmic bytes per
+    query: 2 * ITERS * (4 + 4 * len) (an SA entry and the compared tokens
+    per probe of both bounds)."""
+    import math
+    import torch
+    from suffixgpu_b200 import ops
+    n = tok.numel()
+    rng = np.random.default_rng(44)
+    caps = (32, 16, 8, 4, 2)
+    nq = 1000
+    host = tok.cpu().numpy()
+    pats = np.zeros((nq * len(caps), 32), dtype=np.int32)
+    plen = np.zeros(nq * len(caps), dtype=np.int64)
+    for i, c in enumerate(caps):
+        st = rng.integers(0, n - c, size=nq)
+        pats[i * nq:(i + 1) * nq, :c] = host[st[:, None] + np.arange(c)]
+        plen[i * nq:(i + 1) * nq] = c
+    pat = torch.from_numpy(pats).to(dev)
+    pl = torch.from_numpy(plen).to(dev)
+    for _ in range(3):
+        start, end = ops.search_interval(sa, tok, pat, pl)
+    torch.cuda.synchronize()
+    reps = 20
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        start, end = ops.search_interval(sa, tok, pat, pl)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    found = int((end > start).sum().item())
+    iters = math.ceil(math.log2(n + 1))
+    alg = float(sum(2 * iters * (4 + 4 * c) * nq for c in caps))
+    achieved = alg / (ms * 1e-3) / 1e9
+    return {"metric": "sa_search queries/s", "value": len(plen) / (ms * 1e-3),
+            "unit": "queries/s", "queries_per_launch": len(plen),
+            "us_per_launch": ms * 1e3, "all_found": found == len(plen),
+            "roofline": {"bound": "hbm (latency-bound probes)",
+                         "achieved": achieved, "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                         "alg_bytes_per_launch": alg}}
+
+
+def run_global(args, dev) -> dict:
+    """global memory enabled (capacity 2^22, delta
+    2^16, rebuild threshold 32768), corpus of 4096 template documents x
+    1024 tokens pre-filled through harvest_rows, then B=64 x S=4096 query
+    rows decoded step by step. Every step harvests 4 finished rows of the
+    batch into the delta, polls, and runs propose_with_update; rebuilds run
+    on the side stream from the host worker thread and swap in at a poll.
+    The loop is timed with CUDA events (the host's Python bookkeeping is
+    inside). The propose step alone is also replayed from a CUDA graph."""
+    import torch
+    from suffixgpu_b200 import SuffixGPUDrafter
+    from suffixgpu_b200 import workloads as wl
+    steps = args.global_warmup + args.global_steps
+    data = wl.config3(seed=3, steps=steps)
+    b, s = data["token_ids"].shape
+    d = SuffixGPUDrafter(k=16, device=dev, max_pattern_len=32,
+                         max_occurrences=128, num_backoff=8,
+                         enable_global=True, global_capacity=1 << 22,
+                         delta_capacity=1 << 16, rebuild_threshold=32768,
+                         rebuild_stream=torch.cuda.Stream(dev))
+    gi = d.global_index
+    docs = torch.from_numpy(data["corpus_docs"]).to(dev)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    per = 16
+    for i in range(0, docs.shape[0], per):
+        d.harvest_rows([docs[j] for j in range(i, min(i + per, docs.shape[0]))],
+                       [docs.shape[1]] * min(per, docs.shape[0] - i))
+        gi.wait_rebuild()  # no document dropped while pre-filling
+    gi.wait_rebuild()
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    prefill_rebuilds = gi.rebuilds
+    tok = torch.from_numpy(data["token_ids"]).to(dev)
+    n = torch.from_numpy(data["num_tokens"]).to(dev)
+    q_host = data["num_tokens"].astype(int).tolist()
+    samp = [torch.from_numpy(x).to(dev) for x in data["sampled"]]
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    r0 = 0
+    t1 = 0.0
+    for j in range(steps):
+        if j == args.global_warmup:
+            torch.cuda.synchronize()
+            r0 = gi.rebuilds
+            t1 = time.perf_counter()
+            e0.record()
+        rows = [(4 * j + i) % b for i in range(4)]
+        d.harvest_finished(rows, [q_host[r] for r in rows], tok)
+        d.poll()
+        draft, nv, n = d.propose_with_update(n, tok, samp[j])
+    e1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t1
+    ms = e0.elapsed_time(e1) / args.global_steps
+    rebuilds = gi.rebuilds - r0
+    gi.wait_rebuild()
+    # the propose step alone, replayed from a CUDA graph (no harvest)
+    n_g = torch.from_numpy(data["num_tokens"]).to(dev)
+    tok_g = tok.clone()
+    sg = torch.cuda.Stream(dev)
+    sg.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(sg):
+        for _ in range(3):
+            d.propose(n_g, tok_g)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=sg):
+        for _ in range(10):
+            d.propose(n_g, tok_g)
+    graph.replay()
+    torch.cuda.synchronize()
+    g0 = torch.cuda.Event(enable_timing=True)
+    g1 = torch.cuda.Event(enable_timing=True)
+    g0.record()
+    for _ in range(10):
+        graph.replay()
+    g1.record()
+    torch.cuda.synchronize()
+    graph_us = g0.elapsed_time(g1) * 1e3 / 100
+    del graph
+    return {"metric": "propose_with_update rows/s, global enabled",
+            "value": b / (ms * 1e-3), "unit": "rows/s",
+            "ms_per_step": ms, "wall_ms_per_step":
+                wall * 1e3 / args.global_steps,
+            "steps": args.global_steps, "warmup": args.global_warmup,
+            "rebuilds_in_timed_steps": rebuilds,
+            "active_corpus_tokens": gi.active_len,
+            "prefill_s": prefill_s, "prefill_rebuilds": prefill_rebuilds,
+            "graph_propose_us": graph_us,
+            "graph_propose_rows_per_s": b / (graph_us * 1e-6),
+            "workload": "config3: 4096 x 1024 template corpus (64 templates "
+                        "x 256, 5% substitution, vocab 32000), B=64, "
+                        "S=4096, k=16, P=32, R=128, capacity 2^22, delta "
+                        "2^16, threshold 32768, 4 harvests + poll per step"}
 
 
 def run_e2e(args, drafter, reps, data, dev, world):
@@ -501,11 +658,11 @@ def main():
     args = parse()
     if args.impl == "reference":
         res = run_reference(args)
-    elif args.mode == "sa":
+    elif args.mode in ("sa", "global"):
         import torch
         dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
         torch.cuda.set_device(dev)
-        res = run_sa(args, dev)
+        res = run_sa(args, dev) if args.mode == "sa" else run_global(args, dev)
     else:
         res = run_ours(args)
     if res is not None:

@@ -204,6 +204,35 @@ def test_delta_and_query_vs_oracle():
             np.testing.assert_array_equal(_host(a), b)
 
 
+@pytest.mark.parametrize("delta_capacity,rows,max_len", [
+    (1 << 16, 64, 32),   # config 3: one 8-CTA cluster per row
+    ((1 << 17) + 5, 6, 16),  # an eighth too large for shared memory: tiles
+])
+def test_delta_full_size_vs_oracle(delta_capacity, rows, max_len):
+    """_delta_match_backoff at the config-3 delta capacity, filled with
+    template documents to a little under capacity (plus a capacity above
+    the one-pass limit), against the oracle for every cap of the drafter."""
+    from suffixgpu_b200 import workloads as wl
+    rng = np.random.default_rng(13)
+    z = wl.Zipf(1.1, 32000)
+    templates = z.draw(rng, (64, 256))
+    docs = wl.template_docs(rng, delta_capacity // 1100, 1024, templates, z)
+    g, o = _index_pair(capacity=1 << 12, delta_capacity=delta_capacity,
+                       k=16, max_occurrences=128,
+                       rebuild_threshold=1 << 30)
+    g.append_documents([_dev(d) for d in docs])
+    o.append_documents(list(docs))
+    assert g.delta_len == o.delta_len
+    q = wl.template_docs(rng, rows, 600, templates, z)
+    qlen = rng.integers(1, 600, size=rows).astype(np.int64)
+    qlen[0] = 0
+    caps = np.array(so.global_caps(max_len, 8), dtype=np.int64)
+    got = g._delta_match_backoff(_dev(q), _dev(qlen), max_len, _dev(caps))
+    exp = o._delta_match_backoff(q, qlen, max_len, caps)
+    for a, b in zip(got, exp):
+        np.testing.assert_array_equal(_host(a), b)
+
+
 def test_rebuild_eviction_overflow_vs_oracle():
     """Small capacities force eviction, delta overflow and whole-doc
     snapshots; corpus, SA and queries stay identical."""
