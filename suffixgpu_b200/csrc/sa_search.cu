@@ -7,10 +7,19 @@
 // ceil(log2(n + 1))-iteration loop with the same midpoint rule and the
 // same comparator (_cmp_pattern, :25-63: corpus tokens past the end read
 // -1, pattern positions past its length always match), so the bounds are
-// identical to the reference's for any SA. The backoff variant searches
-// every suffix length 1..M of each row's tail in one block (one thread per
-// length and bound, tail in shared memory) and keeps, per cap, the longest
-// found length <= cap.
+// identical to the reference's for any SA.
+//
+// One warp runs one bound: lane j holds pattern column j (and j + 32, ...),
+// so a probe reads the suffix's columns with one coalesced load and finds
+// the first mismatch with a ballot. The loop is a chain of dependent
+// memory round trips (SA entry, then its tokens); once every remaining
+// midpoint lies within 32 consecutive SA entries the warp loads those into
+// its lanes, and the remaining probes read only tokens. The backoff variant
+// searches every suffix length 1..M of each row's tail on one cluster of 8
+// CTAs (one warp per length and bound); CTA 0 gathers the intervals through
+// distributed shared memory and keeps, per cap, the longest found length
+// <= cap. Patterns wider than 128 columns use one thread per bound.
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include "sg_common.cuh"
@@ -147,6 +156,213 @@ __global__ void sa_backoff_kernel(const int32_t* __restrict__ sa,
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Warp-per-bound search
+// ---------------------------------------------------------------------------
+namespace cg = cooperative_groups;
+
+constexpr int kSWarps = 8;   // warps per block of the search_interval kernel
+constexpr int kSCG = 8;      // CTAs per row of the backoff cluster kernel
+constexpr int kSMaxCols = 4; // pattern columns per lane (width <= 128)
+
+// _cmp_pattern with lane j holding pattern column j + 32 k in pc[k]
+// (columns >= lim are ignored). Warp-uniform result.
+template <int NC>
+__device__ __forceinline__ int warp_cmp(const int32_t* __restrict__ corpus,
+                                        int64_t n, int64_t pos,
+                                        const int (&pc)[NC], int lim,
+                                        int64_t plen, int M) {
+  const int lane = lane_id();
+  int tok[NC];
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    const int j = lane + 32 * k;
+    tok[k] = 0;
+    if (j < lim) {
+      const int64_t x = pos + j;
+      tok[k] = x < n ? corpus[x] : -1;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    const int j = lane + 32 * k;
+    const unsigned bal = __ballot_sync(SG_FULL_MASK, j < lim && tok[k] != pc[k]);
+    if (bal) {  // first mismatching column: compare token with pattern
+      const int f = __ffs(bal) - 1;
+      const int tv = __shfl_sync(SG_FULL_MASK, tok[k], f);
+      const int pv = __shfl_sync(SG_FULL_MASK, pc[k], f);
+      return tv < pv ? -1 : 1;
+    }
+  }
+  if (plen <= M) return 0;  // every column up to min(plen, M) matched
+  // plen > M: the token at column M against pattern column M - 1
+  const int64_t x = pos + M;
+  const int tv = x < n ? corpus[x] : -1;
+  int src = 0;
+#pragma unroll
+  for (int k = 0; k < NC; ++k)
+    if (k == ((M - 1) >> 5)) src = pc[k];
+  const int pv = __shfl_sync(SG_FULL_MASK, src, (M - 1) & 31);
+  return tv < pv ? -1 : (tv > pv ? 1 : 0);
+}
+
+template <int NC>
+__device__ int64_t warp_bound(const int32_t* __restrict__ sa,
+                              const int32_t* __restrict__ corpus, int64_t n,
+                              int iters, const int (&pc)[NC], int M,
+                              int64_t plen, bool upper) {
+  const int lane = lane_id();
+  const int lim = plen < M ? (plen > 0 ? static_cast<int>(plen) : 0) : M;
+  int64_t lo = 0, hi = n;
+  int64_t base = -1;  // once >= 0: lane i holds sa[base + i]
+  int held = 0;
+  for (int it = 0; it < iters; ++it) {
+    int64_t mid = (lo + hi) >> 1;
+    if (mid > n - 1) mid = n - 1;
+    int pos;
+    if (base >= 0)
+      pos = __shfl_sync(SG_FULL_MASK, held, static_cast<int>(mid - base));
+    else
+      pos = sa[mid];
+    const int c = warp_cmp<NC>(corpus, n, pos, pc, lim, plen, M);
+    if (c < 0 || (upper && c == 0)) {
+      lo = mid + 1;
+    } else {
+      hi = mid;
+    }
+    if (base < 0 && it + 1 < iters) {
+      // From state (lo, hi) every later midpoint lies in [min, max(lo, hi)]
+      // (hi never grows, lo never exceeds the old max + 1): cache that
+      // window once it spans at most 32 entries.
+      const int64_t a = lo < hi ? lo : hi;
+      const int64_t z = lo < hi ? hi : lo;
+      const int64_t bs = a < n - 1 ? a : n - 1;
+      if (z - bs <= 31) {
+        base = bs;
+        const int64_t x = bs + lane;
+        held = x < n ? sa[x] : 0;
+      }
+    }
+  }
+  return lo;
+}
+
+// search_interval: one warp per (pattern row, bound).
+template <int NC>
+__global__ void __launch_bounds__(kSWarps * 32)
+    sa_search_warp_kernel(const int32_t* __restrict__ sa,
+                          const int32_t* __restrict__ corpus, int64_t n,
+                          const int32_t* __restrict__ pat, int M,
+                          const int64_t* __restrict__ plen, int B, int iters,
+                          int64_t* __restrict__ start,
+                          int64_t* __restrict__ end) {
+  const int task = blockIdx.x * kSWarps + warp_id();
+  if (task >= 2 * B) return;  // warp-uniform
+  const int row = task >> 1;
+  const bool upper = task & 1;
+  const int lane = lane_id();
+  int pc[NC];
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    const int j = lane + 32 * k;
+    pc[k] = j < M ? pat[static_cast<int64_t>(row) * M + j] : 0;
+  }
+  const int64_t r = warp_bound<NC>(sa, corpus, n, iters, pc, M, plen[row], upper);
+  if (lane == 0) (upper ? end : start)[row] = r;
+}
+
+// suffix_match_backoff: one cluster of kSCG CTAs per row, one warp per
+// (length, bound); CTA 0 gathers the intervals and selects per cap.
+template <int NC>
+__global__ void __cluster_dims__(kSCG, 1, 1) __launch_bounds__(1024)
+    sa_backoff_cluster_kernel(const int32_t* __restrict__ sa,
+                              const int32_t* __restrict__ corpus, int64_t n,
+                              const int32_t* __restrict__ query, int Q,
+                              const int64_t* __restrict__ qlen, int M,
+                              const int64_t* __restrict__ caps, int C,
+                              const uint8_t* __restrict__ row_mask, int iters,
+                              int64_t* __restrict__ out_len,
+                              int64_t* __restrict__ out_start,
+                              int64_t* __restrict__ out_end) {
+  cg::cluster_group cluster = cg::this_cluster();
+  __shared__ long long s_res[32];       // this CTA's bounds, one per warp
+  __shared__ long long s_all[2 * 128];  // CTA 0: every (length, bound)
+  const int g = static_cast<int>(cluster.block_rank());
+  const int b = blockIdx.x / kSCG;
+  const int wpc = blockDim.x >> 5;
+  const int warp = warp_id(), lane = lane_id();
+  const bool active = !row_mask || row_mask[b];
+  const int64_t ql = qlen[b];
+  const int task = g * wpc + warp;
+  if (task < 2 * M) {
+    const int l = (task >> 1) + 1;  // pattern length
+    const bool upper = task & 1;
+    int64_t r = 0;
+    if (active && l <= ql) {
+      // pattern_l[j] = query[qlen - l + j] for j < l (the gather clamps
+      // indices to the query width like the reference)
+      int pc[NC];
+      const int64_t o = ql - l;
+#pragma unroll
+      for (int k = 0; k < NC; ++k) {
+        const int j = lane + 32 * k;
+        const int64_t x = o + j;
+        pc[k] = j < l ? query[static_cast<int64_t>(b) * Q + (x < Q ? x : Q - 1)] : 0;
+      }
+      r = warp_bound<NC>(sa, corpus, n, iters, pc, M, l, upper);
+    }
+    if (lane == 0) s_res[warp] = r;
+  }
+  cluster.sync();  // every CTA's bounds are published
+  if (g == 0) {
+    for (int i = threadIdx.x; i < 2 * M; i += blockDim.x)
+      s_all[i] = *cluster.map_shared_rank(&s_res[i % wpc], i / wpc);
+  }
+  cluster.sync();  // remote reads done; s_all visible to CTA 0
+  if (g == 0) {
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+      const int64_t cap = caps[c];
+      int64_t best = 0;
+      if (active) {
+        for (int l = 1; l <= M; ++l)
+          if (l <= cap && l <= ql && s_all[2 * l - 1] > s_all[2 * l - 2]) best = l;
+      }
+      const int64_t o = static_cast<int64_t>(b) * C + c;
+      out_len[o] = best;
+      out_start[o] = best > 0 ? s_all[2 * best - 2] : 0;
+      out_end[o] = best > 0 ? s_all[2 * best - 1] : 0;
+    }
+  }
+}
+
+template <int NC>
+static int launch_search_warp(const int32_t* sa, const int32_t* corpus,
+                              int64_t n, const int32_t* pattern, int batch,
+                              int width, const int64_t* plen, int64_t* st,
+                              int64_t* en, cudaStream_t stream) {
+  const int64_t blocks = (2 * static_cast<int64_t>(batch) + kSWarps - 1) / kSWarps;
+  sa_search_warp_kernel<NC><<<static_cast<unsigned>(blocks), kSWarps * 32, 0,
+                              stream>>>(sa, corpus, n, pattern, width, plen,
+                                        batch, sa_iters(n), st, en);
+  return check_launch();
+}
+
+template <int NC>
+static int launch_backoff_cluster(const int32_t* sa, const int32_t* corpus,
+                                  int64_t n, const int32_t* query, int batch,
+                                  int qw, const int64_t* qlen, int M,
+                                  const int64_t* caps, int C,
+                                  const uint8_t* row_mask, int64_t* ol,
+                                  int64_t* os, int64_t* oe,
+                                  cudaStream_t stream) {
+  const int wpc = (2 * M + kSCG - 1) / kSCG;  // <= 32 for M <= 128
+  sa_backoff_cluster_kernel<NC><<<batch * kSCG, wpc * 32, 0, stream>>>(
+      sa, corpus, n, query, qw, qlen, M, caps, C, row_mask, sa_iters(n), ol,
+      os, oe);
+  return check_launch();
+}
+
 }  // namespace sg
 
 using namespace sg;
@@ -160,6 +376,17 @@ extern "C" int sg_sa_search(const int32_t* sa, const int32_t* corpus,
   if (batch == 0) return SG_OK;
   if (!sa || !corpus || !pattern || !pattern_len || !out_start || !out_end)
     return SG_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (width <= 32 * kSMaxCols) {
+    if (width <= 32)
+      return launch_search_warp<1>(sa, corpus, n, pattern, batch, width,
+                                   pattern_len, out_start, out_end, st);
+    if (width <= 64)
+      return launch_search_warp<2>(sa, corpus, n, pattern, batch, width,
+                                   pattern_len, out_start, out_end, st);
+    return launch_search_warp<4>(sa, corpus, n, pattern, batch, width,
+                                 pattern_len, out_start, out_end, st);
+  }
   const int th = 64;
   const size_t smem = static_cast<size_t>(th) * width * 4;
   static int cache[64] = {0};
@@ -184,6 +411,23 @@ extern "C" int sg_suffix_match_backoff(
   if (!sa || !corpus || !query || !query_len || !caps || !out_len ||
       !out_start || !out_end)
     return SG_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (max_len <= 32 * kSMaxCols && static_cast<int64_t>(batch) * kSCG <= INT32_MAX) {
+    if (max_len <= 32)
+      return launch_backoff_cluster<1>(sa, corpus, n, query, batch,
+                                       query_width, query_len, max_len, caps,
+                                       num_caps, row_mask, out_len, out_start,
+                                       out_end, st);
+    if (max_len <= 64)
+      return launch_backoff_cluster<2>(sa, corpus, n, query, batch,
+                                       query_width, query_len, max_len, caps,
+                                       num_caps, row_mask, out_len, out_start,
+                                       out_end, st);
+    return launch_backoff_cluster<4>(sa, corpus, n, query, batch,
+                                     query_width, query_len, max_len, caps,
+                                     num_caps, row_mask, out_len, out_start,
+                                     out_end, st);
+  }
   const int th = 2 * max_len < 1024 ? ((2 * max_len + 31) & ~31) : 1024;
   const size_t smem = 4 * static_cast<size_t>((query_width + 1) & ~1) +
                       16 * static_cast<size_t>(max_len);

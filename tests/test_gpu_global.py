@@ -145,6 +145,77 @@ def test_sa_search_random_vs_oracle():
             np.testing.assert_array_equal(_host(g), x)
 
 
+@pytest.mark.parametrize("width", [8, 40, 70, 140])
+def test_sa_search_widths_vs_oracle(width):
+    """Pattern widths of one, two and four columns per lane and beyond the
+    warp path (one thread per bound); corpora with SEP (-2) and -1 tokens
+    and PAD tails; lengths around the width."""
+    from suffixgpu_b200 import ops
+    rng = np.random.default_rng(50 + width)
+    n = 4000
+    corpus = rng.integers(-2, 3, size=n).astype(np.int32)
+    for _ in range(30):  # long repeats so that matches run deep
+        a, b = (int(x) for x in rng.integers(0, n - 300, size=2))
+        ln = int(rng.integers(50, 300))
+        if b + ln <= n:
+            corpus[b:b + ln] = corpus[a:a + ln]
+    corpus[-5:] = so.PAD_TOKEN
+    sa = so.build_suffix_array(corpus).astype(np.int32)
+    nb = 96
+    pat = rng.integers(-2, 3, size=(nb, width)).astype(np.int32)
+    for i in range(0, nb, 2):
+        st = int(rng.integers(0, n - width))
+        pat[i] = corpus[st:st + width]
+    plen = rng.integers(-1, width + 3, size=nb).astype(np.int64)
+    plen[::5] = width
+    s, e = ops.search_interval(_dev(sa), _dev(corpus), _dev(pat), _dev(plen))
+    es, ee = so.search_interval(sa, corpus, pat, plen)
+    np.testing.assert_array_equal(_host(s), es)
+    np.testing.assert_array_equal(_host(e), ee)
+    q = pat[:40].copy()
+    qlen = rng.integers(-1, width + 2, size=40).astype(np.int64)
+    caps = np.array(sorted({width, max(2, width // 2), 4, 2, 1},
+                           reverse=True), dtype=np.int64)
+    got = ops.suffix_match_backoff(_dev(sa), _dev(corpus), _dev(q),
+                                   _dev(qlen), width, _dev(caps))
+    exp = so.suffix_match_backoff(sa, corpus, q, qlen, width, caps)
+    for g, x in zip(got, exp):
+        np.testing.assert_array_equal(_host(g), x)
+
+
+def test_sa_search_config3_size_vs_oracle():
+    """search_interval and suffix_match_backoff over a 2^22-token template
+    corpus (the config-3 capacity) against the oracle's search on the same
+    SA (built on the GPU; the SA itself is covered by the build tests)."""
+    from suffixgpu_b200 import ops
+    from suffixgpu_b200 import workloads as wl
+    rng = np.random.default_rng(60)
+    z = wl.Zipf(1.1, 32000)
+    templates = z.draw(rng, (64, 256))
+    corpus = wl.template_docs(rng, 4096, 1024, templates, z).reshape(-1)
+    sa_t = ops.build_suffix_array(_dev(corpus))
+    sa = _host(sa_t).astype(np.int32)
+    pat = np.zeros((200, 32), dtype=np.int32)
+    plen = np.zeros(200, dtype=np.int64)
+    for i in range(200):
+        ln = int(rng.integers(1, 33))
+        st = int(rng.integers(0, corpus.size - ln))
+        pat[i, :ln] = corpus[st:st + ln]
+        plen[i] = ln if i % 7 else ln + 1
+    s, e = ops.search_interval(_dev(sa), _dev(corpus), _dev(pat), _dev(plen))
+    es, ee = so.search_interval(sa, corpus, pat, plen)
+    np.testing.assert_array_equal(_host(s), es)
+    np.testing.assert_array_equal(_host(e), ee)
+    q = wl.template_docs(rng, 16, 300, templates, z)
+    qlen = rng.integers(0, 300, size=16).astype(np.int64)
+    caps = np.array(so.global_caps(32, 8), dtype=np.int64)
+    got = ops.suffix_match_backoff(_dev(sa), _dev(corpus), _dev(q),
+                                   _dev(qlen), 32, _dev(caps))
+    exp = so.suffix_match_backoff(sa, corpus, q, qlen, 32, caps)
+    for g, x in zip(got, exp):
+        np.testing.assert_array_equal(_host(g), x)
+
+
 # ---------------------------------------------------------------------------
 # global index
 # ---------------------------------------------------------------------------
