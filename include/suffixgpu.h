@@ -257,6 +257,28 @@ int sg_global_combine(int32_t* draft, int32_t* num_valid,
                       const float* g_score, int32_t batch, int32_t num_caps,
                       int32_t k, sg_stream_t stream);
 
+/* The global half of SuffixGPUDrafter.propose after the two searches
+ * (proposer.py:246-320), fused per row: sg_global_candidates' plan and
+ * continuations (kept on chip, never written out), expand_chain with the
+ * drafter's min_token_prob / alpha stopped at each candidate's spec cap,
+ * and sg_global_combine's selection against the local winner in draft /
+ * num_valid / local_score. Inputs are sg_suffix_match_backoff's and
+ * sg_delta_match_backoff's outputs. max_occ <= 1024, k <= 64; returns
+ * SG_ERR_UNSUPPORTED when the row's continuation block
+ * (num_caps * max_occ * k int32 plus vote scratch) exceeds shared memory,
+ * in which case the three separate calls apply. */
+int sg_global_draft(const int64_t* sa_len, const int64_t* sa_start,
+                    const int64_t* sa_end, const int64_t* d_len,
+                    const int64_t* d_pos, const int64_t* d_cnt,
+                    const int32_t* sa, const int32_t* corpus,
+                    int64_t capacity, const int32_t* delta,
+                    int64_t delta_capacity, const int64_t* delta_len,
+                    int32_t batch, int32_t num_caps, int32_t max_occ,
+                    int32_t k, int32_t has_spec_factor, float spec_factor,
+                    float spec_offset, float min_token_prob, float alpha,
+                    const float* local_score, const uint8_t* row_mask,
+                    int32_t* draft, int32_t* num_valid, sg_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

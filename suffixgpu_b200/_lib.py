@@ -99,6 +99,12 @@ _SIGS: dict[str, list] = {
     "sg_global_combine": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                           c_void_p, c_void_p, c_int32, c_int32, c_int32,
                           c_void_p],
+    "sg_global_draft": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                        c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
+                        c_int64, c_void_p, c_int32, c_int32, c_int32,
+                        c_int32, c_int32, c_float, c_float, c_float,
+                        c_float, c_void_p, c_void_p, c_void_p, c_void_p,
+                        c_void_p],
 }
 
 
@@ -146,7 +152,11 @@ def register(name: str, argtypes: list, restype=c_int) -> None:
 
 def call(name: str, *args) -> None:
     """Call an entry point; raise on a non-zero status."""
-    st = getattr(lib(), name)(*args)
+    check(name, getattr(lib(), name)(*args))
+
+
+def check(name: str, st: int) -> None:
+    """Raise for a non-zero status returned by entry point ``name``."""
     if st != 0:
         L = lib()
         msg = L.sg_status_string(st).decode()
@@ -163,5 +173,5 @@ def stream_of(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
-__all__ = ["DraftParams", "LocalInputs", "LocalOutputs", "lib", "call", "ptr",
-           "stream_of", "register", "c_size_t"]
+__all__ = ["DraftParams", "LocalInputs", "LocalOutputs", "lib", "call",
+           "check", "ptr", "stream_of", "register", "c_size_t"]

@@ -147,6 +147,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// Ampere-style asynchronous 4-byte copy global -> shared (no register
+// staging; completion per thread with cp_async_wait_all, which also orders
+// the copies against later accesses, so the copy itself carries no memory
+// clobber and does not hold back unrelated loads).
+__device__ __forceinline__ void cp_async_4(void* dst_smem, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst_smem)),
+               "l"(src));
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 // Device-side error word: kernels OR error bits into it; the host reads it
 // back in tests. Bit 0: a bounded wait timed out.
 constexpr int kDevErrWait = 1;

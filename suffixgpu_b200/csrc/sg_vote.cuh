@@ -16,7 +16,7 @@
 // slot and votes:
 //   * <= 32 survivors (one per lane): each lane counts its token among the
 //     32 in a shared buffer (8 vector loads), then two warp reductions;
-//   * more: the first voting token is counted with ballots and wins on a
+//   * more: the median voter's token is counted with ballots and wins on a
 //     strict majority; otherwise the other tokens go through a per-warp
 //     open-addressing table in shared memory, one CAS insert + one atomic
 //     add per token, all of a lane's in flight together; every lane then
@@ -154,30 +154,45 @@ __device__ __forceinline__ void vote_hash(const int (&v)[RJ], int nslots,
   __syncwarp();
 }
 
-// Plurality vote over RJ slots per lane. The first voting token (the
-// leader) is counted with ballots; a strict majority wins outright. Only
-// otherwise do the remaining tokens go through the hash table, with the
-// leader's tokens left out: copies make one continuation dominate, and
-// inserting 32 equal keys serialises the table's atomics on one slot.
+// Plurality vote over RJ slots per lane. The token of the median voter (in
+// occurrence order) is the leader and is counted with ballots; a strict
+// majority wins outright. Only otherwise do the remaining tokens go
+// through the hash table, with the leader's tokens left out: copies make
+// one continuation dominate, and inserting 32 equal keys serialises the
+// table's atomics on one slot. The median, not the first voter: suffix-
+// array samples come in lexicographic order, so the survivors' tokens at
+// a depth are sorted and a majority token always covers the middle.
 template <int RJ>
 __device__ __forceinline__ void vote_multi(const int (&v)[RJ], int nslots,
                                            const VoteScratch& vs,
                                            int& best_cnt, int& best_tok,
                                            int& n_act) {
-  int ref = -1, na = 0;
+  const unsigned lt_mask = (1u << lane_id()) - 1u;
+  unsigned bal[RJ];
+  int na = 0;
 #pragma unroll
   for (int j = 0; j < RJ; ++j) {
-    if (j < nslots) {
-      const unsigned bal = __ballot_sync(SG_FULL_MASK, v[j] != -1);
-      na += __popc(bal);
-      if (ref == -1 && bal) ref = __shfl_sync(SG_FULL_MASK, v[j], __ffs(bal) - 1);
-    }
+    bal[j] = j < nslots ? __ballot_sync(SG_FULL_MASK, v[j] != -1) : 0u;
+    na += __popc(bal[j]);
   }
   n_act = na;
   if (na == 0) {
     best_cnt = 0;
     best_tok = INT32_MAX;
     return;
+  }
+  const int target = na >> 1;  // 0-based rank of the median voter
+  int ref = -1, before = 0;
+#pragma unroll
+  for (int j = 0; j < RJ; ++j) {
+    const int cj = __popc(bal[j]);
+    if (ref == -1 && before + cj > target) {
+      const bool me = ((bal[j] >> lane_id()) & 1u) &&
+                      __popc(bal[j] & lt_mask) == target - before;
+      const unsigned sel = __ballot_sync(SG_FULL_MASK, me);
+      ref = __shfl_sync(SG_FULL_MASK, v[j], __ffs(sel) - 1);
+    }
+    before += cj;
   }
   int cr = 0;
 #pragma unroll

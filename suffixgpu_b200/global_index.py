@@ -23,10 +23,11 @@ from collections import deque
 import torch
 
 from suffixgpu_b200 import ops
-from suffixgpu_b200._lib import call, ptr, stream_of
+from suffixgpu_b200._lib import call, check, lib, ptr, stream_of
 
 PAD_TOKEN = torch.iinfo(torch.int32).max
 SEP_TOKEN = -2
+_UNSUPPORTED = 4  # SG_ERR_UNSUPPORTED
 
 
 class _ThreadEvent:
@@ -304,18 +305,28 @@ class GlobalIndex:
         """Per-cap matches against corpus + delta: (match_len [B, C] i64,
         cont [B, C, R, k] int32, occ_count [B, C] i64) and, with
         spec=(has_factor, factor, offset), the spec caps [B, C] i64."""
-        dev = self.device
         query = ops.as_i32(query)
         query_len = ops.as_i64(query_len)
         caps = ops.as_i64(caps)
-        b = query.shape[0]
-        cnum = caps.numel()
-        r = self.max_occurrences
+        found = self._searches(query, query_len, max_len, caps, row_mask)
+        return self._candidates(found, query.shape[0], caps.numel(), spec)
+
+    def _searches(self, query, query_len, max_len: int, caps, row_mask):
+        """SA walk and delta scan per cap (global_index.py:286-320):
+        (sa_len, sa_start, sa_end, d_len, d_pos, d_cnt)."""
         sa_len, sa_start, sa_end = ops.suffix_match_backoff(
             self.sa, self.corpus, query, query_len, max_len, caps,
             row_mask=row_mask)
         d_len, d_pos, d_cnt = self._delta_match_backoff(
             query, query_len, max_len, caps, row_mask=row_mask)
+        return sa_len, sa_start, sa_end, d_len, d_pos, d_cnt
+
+    def _candidates(self, found, b: int, cnum: int, spec=None):
+        """The tail of _query_backoff (global_index.py:321-370) and
+        _gather_cont (:443-463) on the search results."""
+        dev = self.device
+        r = self.max_occurrences
+        sa_len, sa_start, sa_end, d_len, d_pos, d_cnt = found
         match_len = torch.empty(b, cnum, dtype=torch.int64, device=dev)
         cont = torch.empty(b, cnum, r, self.k, dtype=torch.int32, device=dev)
         occ = torch.empty(b, cnum, dtype=torch.int64, device=dev)
@@ -421,15 +432,30 @@ class GlobalIndex:
         spec = (drafter.max_spec_factor is not None,
                 drafter.max_spec_factor or 0.0, drafter.max_spec_offset)
         row_mask = local["row_mask"]
-        match_len, cont, occ, cap = self._query_backoff(
-            tails, tail_len, p, caps, row_mask=row_mask, spec=spec)
         cnum = caps.numel()
+        found = self._searches(tails, tail_len, p, caps, row_mask)
+        draft, nv = local["draft"], local["num_valid"]
+        # fused candidates + expand + selection (continuations on chip);
+        # the continuation width must be the draft length
+        st_code = _UNSUPPORTED if self.k != drafter.k else lib().sg_global_draft(
+            *(ptr(x) for x in found[:6]), ptr(self.sa), ptr(self.corpus),
+            self.capacity, ptr(self.delta), self.delta_capacity,
+            ptr(self.delta_len_t), b, cnum, self.max_occurrences, drafter.k,
+            int(spec[0]), float(spec[1]), float(spec[2]),
+            float(drafter.min_token_prob),
+            float(drafter.vote_smoothing_alpha), ptr(local["best_score"]),
+            ptr(row_mask), ptr(draft), ptr(nv), st)
+        if st_code == 0:
+            return draft, nv
+        if st_code != _UNSUPPORTED:
+            check("sg_global_draft", st_code)
+        # the row's continuation block does not fit on chip: separate steps
+        match_len, cont, occ, cap = self._candidates(found, b, cnum, spec)
         chain, _, emit, score = ops.expand_chain(
             cont.reshape(b * cnum, self.max_occurrences, self.k),
             occ.reshape(-1), drafter.k,
             min_token_prob=drafter.min_token_prob, cap=cap.reshape(-1),
             alpha=drafter.vote_smoothing_alpha)
-        draft, nv = local["draft"], local["num_valid"]
         call("sg_global_combine", ptr(draft), ptr(nv),
              ptr(local["best_score"]), ptr(row_mask), ptr(chain), ptr(emit),
              ptr(score), b, cnum, drafter.k, st)

@@ -245,6 +245,54 @@ def test_global_scenarios_vs_oracle(seed):
         np.testing.assert_array_equal(got[key], exp[key], key)
 
 
+class _NoFusedDraft:
+    """The kernel library with sg_global_draft answering "unsupported", as
+    it does when a row's continuation block exceeds shared memory."""
+
+    def __init__(self, real):
+        self._real = real
+
+    def sg_global_draft(self, *args):
+        return 4
+
+    def __getattr__(self, name):
+        return getattr(self._real, name)
+
+
+@pytest.mark.parametrize("seed", [41, 42])
+def test_global_scenarios_unfused_match_goldens(golden_dir, seed,
+                                                monkeypatch):
+    """The separate candidates / expand / combine steps (taken when the
+    fused global step does not fit on chip) give the same drafts."""
+    from suffixgpu_b200 import _lib, global_index
+    real = _lib.lib()
+    monkeypatch.setattr(global_index, "lib", lambda: _NoFusedDraft(real))
+    z = np.load(os.path.join(golden_dir, f"global_{seed}.npz"))
+    sc = scenarios.global_scenario(seed)
+    got = scenarios.run_scenario(sc, _gpu_drafter, _dev, _host)
+    for key in ("draft", "num_valid", "new_counts"):
+        np.testing.assert_array_equal(got[key], z["out_" + key], key)
+
+
+def test_global_draft_rejects_oversized_rows():
+    """sg_global_draft returns SG_ERR_UNSUPPORTED (no launch) when the
+    continuation block of a row cannot fit in shared memory."""
+    import ctypes
+    from suffixgpu_b200 import _lib
+    L = _lib.lib()
+    i64 = torch.zeros(16 * 1024, dtype=torch.int64, device=DEV)
+    i32 = torch.zeros(16 * 1024, dtype=torch.int32, device=DEV)
+    f32 = torch.zeros(4, dtype=torch.float32, device=DEV)
+    p64, p32 = i64.data_ptr(), i32.data_ptr()
+    st = L.sg_global_draft(p64, p64, p64, p64, p64, p64, p32, p32, 1024, p32,
+                           1024, p64, 1, 16, 1024, 64, 0,
+                           ctypes.c_float(0.0), ctypes.c_float(0.0),
+                           ctypes.c_float(0.0), ctypes.c_float(0.0),
+                           f32.data_ptr(), None, p32, p32,
+                           torch.cuda.current_stream().cuda_stream)
+    assert st == 4
+
+
 def _index_pair(**kw):
     from suffixgpu_b200.global_index import GlobalIndex
     return GlobalIndex(device=DEV, **kw), so.GlobalIndex(**kw)
