@@ -588,6 +588,38 @@ class GlobalIndex:
             n_new, new_doc_lens = self._pending
             self._finish_swap(n_new, new_doc_lens)
 
+    def load_documents(self, docs) -> None:
+        """Bulk form of harvesting (the product's GlobalIndex.load_documents;
+        no reference counterpart), stated literally: the documents (each
+        trimmed to its last capacity - 1 tokens so that it fits with its SEP)
+        go to an otherwise empty, unbounded delta, and the reference's
+        rebuild (global_index.py:147-223) runs until the delta is empty."""
+        if self.delta_len:
+            raise ValueError("load_documents needs an empty delta")
+        docs = [np.asarray(d).astype(np.int32).reshape(-1) for d in docs]
+        docs = [d[-(self.capacity - 1):] for d in docs if d.size > 0]
+        saved_cap = self.delta_capacity
+        total = sum(d.size + 1 for d in docs)
+        self.delta = np.zeros(max(total, 1), dtype=np.int32)
+        self.delta_capacity = self.delta.size
+        for d in docs:
+            n = d.size
+            self.delta[self.delta_len:self.delta_len + n] = d
+            self.delta[self.delta_len + n] = SEP_TOKEN
+            self.delta_len += n + 1
+            self.delta_doc_lens.append(n + 1)
+        self.delta_len_t = self.delta_len
+        while self.delta_len > 0:
+            before = self.delta_len
+            self._launch_rebuild()
+            if self.delta_len == before:
+                break
+        self.delta = np.zeros(saved_cap, dtype=np.int32)
+        self.delta_capacity = saved_cap
+        self.delta_len = 0
+        self.delta_len_t = 0
+        self.delta_doc_lens = []
+
     # queries (global_index.py:257-370, 443-553)
     def query(self, query, query_len, max_len):
         caps = np.array([max_len], dtype=np.int64)

@@ -30,6 +30,56 @@ SEP_TOKEN = -2
 _UNSUPPORTED = 4  # SG_ERR_UNSUPPORTED
 
 
+def plan_bulk_load(active_doc_lens, active_len: int, new_doc_lens,
+                   capacity: int):
+    """Host bookkeeping of a bulk load: the documents of ``new_doc_lens``
+    (each length counting its SEP) are appended to an otherwise empty delta
+    and rebuilds run (global_index.py:147-223 rules: evict the oldest whole
+    active documents until active + delta fit, absorb the oldest whole
+    delta documents that fit) until the delta is empty. Returns
+    (keep_tokens, first_new, n_new_docs, rebuilds): the final corpus is the
+    last ``keep_tokens`` tokens of the current active corpus followed by
+    new documents ``first_new .. first_new + n_new_docs - 1``."""
+    act = list(active_doc_lens)       # lengths of the current corpus docs
+    src = [0] * len(act)              # 0 = old active doc, 1 = new doc
+    idx = list(range(len(act)))       # index within its source
+    delta = list(range(len(new_doc_lens)))
+    dlen = sum(new_doc_lens)
+    alen = active_len
+    rebuilds = 0
+    while delta:
+        keep = 0
+        drop = 0
+        for ln in act:
+            if alen - keep + dlen <= capacity:
+                break
+            keep += ln
+            drop += 1
+        n_keep = alen - keep
+        room = capacity - n_keep
+        take = 0
+        acc = 0
+        for j in delta:
+            if acc + new_doc_lens[j] <= min(dlen, room):
+                acc += new_doc_lens[j]
+                take += 1
+            else:
+                break
+        if n_keep + acc == 0:
+            break  # nothing fits (a document longer than the capacity)
+        act = act[drop:] + [new_doc_lens[j] for j in delta[:take]]
+        src = src[drop:] + [1] * take
+        idx = idx[drop:] + delta[:take]
+        delta = delta[take:]
+        dlen -= acc
+        alen = n_keep + acc
+        rebuilds += 1
+    old = [ln for ln, s in zip(act, src) if s == 0]
+    new = [i for i, s in zip(idx, src) if s == 1]
+    first_new = new[0] if new else len(new_doc_lens)
+    return sum(old), first_new, len(new), rebuilds
+
+
 class _ThreadEvent:
     """Completion flag of a background build (query() like a CUDA event)."""
 
@@ -86,6 +136,9 @@ class GlobalIndex:
         self.rebuilds = 0
         self.last_rounds = 0
         self._sa_ws: torch.Tensor | None = None
+        # Multi-GPU: maps "my rebuild has finished" to "every rank's has",
+        # so that replicas of the index swap at the same call.
+        self.rebuild_agree = None
 
     # ------------------------------------------------------------------
     # writes (global_index.py:86-133)
@@ -268,7 +321,10 @@ class GlobalIndex:
         """Swap in a finished background rebuild (non-blocking)."""
         if self._rebuild_event is None:
             return
-        if self._rebuild_event.query():
+        done = self._rebuild_event.query()
+        if self.rebuild_agree is not None:
+            done = self.rebuild_agree(done)
+        if done:
             err = getattr(self._rebuild_event, "error", None)
             if err is not None:
                 self._rebuild_event = None
@@ -277,6 +333,103 @@ class GlobalIndex:
                     from err
             n_new, new_doc_lens = self._pending
             self._finish_swap(n_new, new_doc_lens)
+
+    # ------------------------------------------------------------------
+    # bulk load and persistence (no reference counterpart; the reference
+    # lists "global tree save & load" as a TODO, README.md:212-217)
+    # ------------------------------------------------------------------
+    def load_documents(self, docs: list[torch.Tensor]) -> None:
+        """Load many finished documents at once: the state equals appending
+        them (each trimmed to its last capacity - 1 tokens, so that it fits
+        with its SEP) to an otherwise empty, unbounded delta and running the
+        rebuild (eviction and snapshot rules of global_index.py:147-223)
+        until the delta is empty. One suffix-array build, synchronous."""
+        self.wait_rebuild()
+        if self.delta_len:
+            raise ValueError("load_documents needs an empty delta")
+        cap = self.capacity
+        docs = [d.to(self.device).to(torch.int32).reshape(-1) for d in docs]
+        docs = [d[-(cap - 1):] for d in docs if d.numel() > 0]
+        if not docs:
+            return
+        new_lens = [int(d.numel()) + 1 for d in docs]
+        keep, first, count, rounds = plan_bulk_load(
+            self.active_doc_lens, self.active_len, new_lens, cap)
+        if rounds == 0:
+            return
+        offs = [0]
+        for ln in new_lens:
+            offs.append(offs[-1] + ln)
+        n_tail = offs[first + count] - offs[first]
+        n_new = keep + n_tail
+        dst = self.staging_corpus
+        dst.fill_(PAD_TOKEN)
+        if keep > 0:
+            dst[:keep].copy_(self.corpus[self.active_len - keep:self.active_len])
+        if count:
+            sep = torch.full((1,), SEP_TOKEN, dtype=torch.int32,
+                             device=self.device)
+            parts = []
+            for d in docs[first:first + count]:
+                parts.append(d)
+                parts.append(sep)
+            dst[keep:n_new].copy_(torch.cat(parts))
+        new_doc_lens: deque[int] = deque()
+        acc = 0
+        kept_old = []
+        for ln in reversed(self.active_doc_lens):
+            if acc >= keep:
+                break
+            kept_old.append(ln)
+            acc += ln
+        new_doc_lens.extend(reversed(kept_old))
+        new_doc_lens.extend(new_lens[first:first + count])
+        if self._sa_ws is None:
+            from suffixgpu_b200 import _lib
+            need = int(_lib.lib().sg_suffix_array_workspace_size(cap))
+            self._sa_ws = torch.empty(need, dtype=torch.uint8,
+                                      device=self.device)
+        self._build_staging_sa(dst, min(n_new + 1, cap), None)
+        self._finish_swap(n_new, new_doc_lens)
+
+    def state_dict(self) -> dict:
+        """Corpus, suffix array, delta and document lengths as host tensors
+        (raw int32 arrays plus length lists), for torch.save. Waits for an
+        in-flight rebuild first."""
+        self.wait_rebuild()
+        n = self.active_len
+        return {
+            "capacity": self.capacity,
+            "delta_capacity": self.delta_capacity,
+            "corpus": self.corpus[:n].cpu(),
+            "sa": self.sa[:min(n + 1, self.capacity)].cpu(),
+            "delta": self.delta[:self.delta_len].cpu(),
+            "active_doc_lens": list(self.active_doc_lens),
+            "delta_doc_lens": list(self.delta_doc_lens),
+        }
+
+    def load_state_dict(self, state: dict) -> None:
+        """Restore a state_dict() of an index with the same capacities into
+        the existing device buffers (tensor identity is kept, so captured
+        CUDA graphs stay valid); no rebuild runs."""
+        if (int(state["capacity"]) != self.capacity
+                or int(state["delta_capacity"]) != self.delta_capacity):
+            raise ValueError("state_dict capacities differ from this index")
+        self.wait_rebuild()
+        corpus = state["corpus"].to(torch.int32)
+        sa = state["sa"].to(torch.int32)
+        delta = state["delta"].to(torch.int32)
+        n = corpus.numel()
+        self.corpus.fill_(PAD_TOKEN)
+        self.corpus[:n].copy_(corpus)
+        self.sa.copy_(self._arange)
+        self.sa[:sa.numel()].copy_(sa)
+        self.delta[:delta.numel()].copy_(delta)
+        self.delta_len = int(delta.numel())
+        self.delta_len_t.fill_(self.delta_len)
+        self.active_len = n
+        self.active_doc_lens = deque(int(x) for x in state["active_doc_lens"])
+        self.delta_doc_lens = [int(x) for x in state["delta_doc_lens"]]
 
     def wait_rebuild(self) -> None:
         """Block until an in-flight background rebuild has finished and

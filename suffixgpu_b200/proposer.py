@@ -157,9 +157,15 @@ class SuffixGPUDrafter:
 
     def harvest_rows(self, rows: list[torch.Tensor],
                      lengths: list[int]) -> None:
-        if self.global_index is None or not rows:
+        if self.global_index is None:
             return
         docs = [row[:ln] for row, ln in zip(rows, lengths) if ln > 0]
+        self._append_docs(docs)
+
+    def _append_docs(self, docs: list[torch.Tensor]) -> None:
+        """Documents into the global index; nothing happens for none
+        (proposer.py:351-352, 384-385). The multi-GPU drafter exchanges
+        them between ranks here."""
         if docs:
             self.global_index.append_documents(docs)
 
@@ -178,8 +184,7 @@ class SuffixGPUDrafter:
                 self._ingested[key] = ln
             if final:
                 self._ingested.pop(key, None)
-        if docs:
-            self.global_index.append_documents(docs)
+        self._append_docs(docs)
 
     def load_model(self, *args, **kwargs) -> None:
         pass

@@ -424,3 +424,76 @@ def test_delta_overflow_with_rebuild_in_flight():
         exp = o.query(q, ql, 8)
         for a, b in zip(got, exp):
             np.testing.assert_array_equal(_host(a), b)
+
+
+# ---------------------------------------------------------------------------
+# bulk load and persistence
+# ---------------------------------------------------------------------------
+def _assert_index_equal(g, o):
+    assert g.active_len == o.active_len
+    assert list(g.active_doc_lens) == list(o.active_doc_lens)
+    assert g.delta_len == o.delta_len
+    np.testing.assert_array_equal(_host(g.corpus), o.corpus)
+    np.testing.assert_array_equal(_host(g.sa), o.sa)
+    np.testing.assert_array_equal(_host(g.delta[:g.delta_len]),
+                                  o.delta[:o.delta_len])
+
+
+def test_load_documents_vs_oracle():
+    """Two bulk loads (the second evicting part of the first), then normal
+    harvesting with rebuilds: corpus, SA, document lengths and queries stay
+    identical to the oracle's literal repeated-rebuild process."""
+    rng = np.random.default_rng(71)
+    g, o = _index_pair(capacity=700, delta_capacity=120, k=5,
+                       max_occurrences=12, rebuild_threshold=60)
+    for n_docs in (9, 14):
+        docs = [rng.integers(0, 6, size=int(rng.integers(1, 90))).astype(
+            np.int32) for _ in range(n_docs)]
+        docs.append(rng.integers(0, 6, size=730).astype(np.int32))  # trimmed
+        g.load_documents([_dev(d) for d in docs])
+        o.load_documents(docs)
+        _assert_index_equal(g, o)
+    q = rng.integers(0, 6, size=(20, 10)).astype(np.int32)
+    qlen = rng.integers(0, 11, size=20).astype(np.int64)
+    for a, b in zip(g.query(_dev(q), _dev(qlen), 8), o.query(q, qlen, 8)):
+        np.testing.assert_array_equal(_host(a), b)
+    more = [rng.integers(0, 6, size=int(rng.integers(5, 40))).astype(np.int32)
+            for _ in range(6)]
+    g.append_documents([_dev(d) for d in more])
+    o.append_documents(more)
+    _assert_index_equal(g, o)
+
+
+def test_state_dict_round_trip():
+    """state_dict -> torch.save -> load_state_dict into a fresh index gives
+    the same corpus, SA, delta and queries, and later harvesting and
+    rebuilds continue identically."""
+    import io
+    from suffixgpu_b200.global_index import GlobalIndex
+    rng = np.random.default_rng(72)
+    kw = dict(capacity=900, delta_capacity=200, k=5, max_occurrences=12,
+              rebuild_threshold=100)
+    g = GlobalIndex(device=DEV, **kw)
+    docs = [_dev(rng.integers(0, 7, size=int(rng.integers(5, 70))).astype(
+        np.int32)) for _ in range(12)]
+    g.append_documents(docs)
+    assert g.active_len > 0 and g.delta_len > 0
+    buf = io.BytesIO()
+    torch.save(g.state_dict(), buf)
+    buf.seek(0)
+    h = GlobalIndex(device=DEV, **kw)
+    h.load_state_dict(torch.load(buf))
+    for name in ("corpus", "sa"):
+        assert torch.equal(getattr(g, name), getattr(h, name)), name
+    assert torch.equal(g.delta[:g.delta_len], h.delta[:h.delta_len])
+    assert list(g.active_doc_lens) == list(h.active_doc_lens)
+    assert g.delta_doc_lens == h.delta_doc_lens
+    q = _dev(rng.integers(0, 7, size=(16, 9)).astype(np.int32))
+    qlen = _dev(rng.integers(0, 10, size=16).astype(np.int64))
+    for a, b in zip(g.query(q, qlen, 8), h.query(q, qlen, 8)):
+        assert torch.equal(a, b)
+    more = [_dev(rng.integers(0, 7, size=30).astype(np.int32))
+            for _ in range(5)]
+    g.append_documents(more)
+    h.append_documents(more)
+    assert torch.equal(g.corpus, h.corpus) and torch.equal(g.sa, h.sa)
