@@ -57,10 +57,11 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true",
                     help="skip the CPU baseline leg (profiling runs)")
     ap.add_argument("--mode", default="draft",
-                    choices=["draft", "sa", "global"],
+                    choices=["draft", "sa", "global", "sharded"],
                     help="draft: config 2 (+ SA build, SA query and "
                          "global-path lines); sa: SA build + queries only "
-                         "(config 4); global: config 3 only")
+                         "(config 4); global: config 3 only; sharded: "
+                         "config 5 only (1..8 GPUs under torchrun)")
     ap.add_argument("--sa-log2n", type=int, default=24,
                     help="SA build size (config 4: 2^24 tokens)")
     ap.add_argument("--sa-reps", type=int, default=5)
@@ -71,6 +72,10 @@ def parse():
     ap.add_argument("--global-steps", type=int, default=60,
                     help="timed decode steps of config 3")
     ap.add_argument("--global-warmup", type=int, default=8)
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the config 5 measurement in draft mode")
+    ap.add_argument("--sharded-steps", type=int, default=512,
+                    help="timed propose steps of config 5 per GPU")
     return ap.parse_args()
 
 
@@ -312,6 +317,10 @@ def run_ours(args):
             res["sa_build"] = run_sa(args, dev)
         if not args.no_global:
             res["global"] = run_global(args, dev)
+    if not args.no_sharded:
+        sh = run_sharded(args, dev, world, rank)  # every rank takes part
+        if rank == 0:
+            res["sharded"] = sh
     if world > 1:
         dist.barrier()
         del full, part
@@ -417,6 +426,101 @@ def run_queries(args, tok, sa, dev, peaks) -> dict:
                          "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                          "alg_bytes_per_launch": alg}}
+
+
+NREP5, DECODE5 = 16, 32
+
+
+def run_sharded(args, dev, world: int, rank: int) -> dict | None:
+    """the global drafter on every GPU of the job, 128
+    query rows (S=16384) per GPU, k=32, P=64, R=256, 8 backoff levels,
+    factor 2.0, min_prob 0.1, over a 2^26-token template corpus (512
+    templates x 512, vocab 128256) that every rank bulk-loads from the same
+    seed (ShardedSuffixDrafter: replicated index, rows per rank; the plain
+    drafter on one GPU). One step = one propose_with_update of the rank's
+    rows; steps replay from a CUDA graph over 16 rotating replicas of the
+    token buffer (128 MiB > L2), each walking a 32-step decode loop. Value:
+    all ranks' rows / max-over-ranks time (weak scaling)."""
+    import torch
+    import torch.distributed as dist
+    from suffixgpu_b200 import SuffixGPUDrafter
+    from suffixgpu_b200 import workloads as wl
+    data = wl.config5(rank=rank, steps=DECODE5)
+    if world > 1:
+        from suffixgpu_b200.distributed import ShardedSuffixDrafter
+        d = ShardedSuffixDrafter(device=dev, **wl.CONFIG5_DRAFTER)
+    else:
+        d = SuffixGPUDrafter(device=dev, **wl.CONFIG5_DRAFTER)
+    docs = torch.from_numpy(data["corpus_docs"]).to(dev)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    d.load_documents(list(docs.unbind(0)))
+    torch.cuda.synchronize()
+    load_s = time.perf_counter() - t0
+    del docs
+    b = data["token_ids"].shape[0]
+    tok0 = torch.from_numpy(data["token_ids"]).to(dev)
+    q0 = torch.from_numpy(data["num_tokens"]).to(dev)
+    samp0 = torch.from_numpy(data["sampled"]).to(dev)
+    reps = []
+    for r in range(NREP5):
+        reps.append({"tok": torch.roll(tok0, 5 * r, 0).contiguous(),
+                     "cnt0": torch.roll(q0, 5 * r, 0).contiguous(),
+                     "samp": torch.roll(samp0, 5 * r, 1).contiguous()})
+    cycle = NREP5 * DECODE5
+
+    def run_seq(n):
+        cur = [rp["cnt0"] for rp in reps]
+        for i in range(n):
+            r, j = i % NREP5, (i // NREP5) % DECODE5
+            if j == 0:
+                cur[r] = reps[r]["cnt0"]
+            _, _, cur[r] = d.propose_with_update(cur[r], reps[r]["tok"],
+                                                 reps[r]["samp"][j])
+
+    run_seq(3 * NREP5)
+    torch.cuda.synchronize()
+    steps = max(1, args.sharded_steps)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        run_seq(min(steps, cycle))
+    graph.replay()
+    torch.cuda.synchronize()
+    reps_needed = max(1, steps // cycle)
+    steps = reps_needed * min(steps, cycle)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps_needed):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms, load_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max, load_max = float(t[0].item()), float(t[1].item())
+    del graph
+    if rank != 0:
+        return None
+    return {"metric": "propose_with_update rows/s, global drafter "
+                      "(config 5)",
+            "value": world * b * steps / (ms_max * 1e-3), "unit": "rows/s",
+            "n_gpus": world, "rows_per_gpu": b, "steps": steps,
+            "ms_per_step": ms_max / steps, "scaling": "weak",
+            "corpus_tokens": int(d.global_index.active_len),
+            "load_s": load_max,
+            "workload": "config5: 128 rows x S=16384 per GPU, k=32, P=64, "
+                        "R=256, 8 backoff, factor 2.0, min_prob 0.1; 2^26-"
+                        "token corpus of 512 x 512 templates (5% "
+                        "substitution, vocab 128256), index replicated on "
+                        "every GPU",
+            "l2": "16 rotating replicas x 8 MiB token buffer"}
 
 
 def run_global(args, dev) -> dict:
@@ -663,6 +767,20 @@ def main():
         dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
         torch.cuda.set_device(dev)
         res = run_sa(args, dev) if args.mode == "sa" else run_global(args, dev)
+    elif args.mode == "sharded":
+        import datetime
+        import torch
+        import torch.distributed as dist
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        torch.cuda.set_device(dev)
+        if world > 1:
+            dist.init_process_group("nccl", device_id=dev,
+                                    timeout=datetime.timedelta(seconds=300))
+        res = run_sharded(args, dev, world, rank)
+        if world > 1:
+            dist.destroy_process_group()
     else:
         res = run_ours(args)
     if res is not None:

@@ -112,8 +112,7 @@ class ShardedSuffixDrafter(SuffixGPUDrafter):
     def load_documents(self, docs: list[torch.Tensor]) -> None:
         """Bulk-load documents that every rank holds (the same list on
         every rank, e.g. generated from a shared seed): no exchange."""
-        if self.global_index is not None:
-            self.global_index.load_documents(docs)
+        super().load_documents(docs)
 
 
 __all__ = ["ShardedSuffixDrafter", "exchange_documents", "agree_all"]

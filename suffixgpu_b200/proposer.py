@@ -186,5 +186,12 @@ class SuffixGPUDrafter:
                 self._ingested.pop(key, None)
         self._append_docs(docs)
 
+    def load_documents(self, docs: list[torch.Tensor]) -> None:
+        """Bulk-load finished documents into the global index
+        (GlobalIndex.load_documents; no reference counterpart)."""
+        if self.global_index is None:
+            raise ValueError("load_documents needs enable_global=True")
+        self.global_index.load_documents(docs)
+
     def load_model(self, *args, **kwargs) -> None:
         pass

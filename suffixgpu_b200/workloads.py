@@ -141,3 +141,28 @@ def config4(seed: int = 4, n: int = 1 << 24, vocab: int = 128256,
         st = rng.integers(0, n - c, size=n_queries)
         queries[c] = tokens[st[:, None] + np.arange(c)[None, :]]
     return {"tokens": tokens, "queries": queries}
+
+
+CONFIG5_DRAFTER = dict(k=32, max_pattern_len=64, max_occurrences=256,
+                       num_backoff=8, enable_global=True,
+                       global_capacity=1 << 26, delta_capacity=1 << 16,
+                       max_spec_factor=2.0, min_token_prob=0.1)
+
+
+def config5(seed: int = 5, rank: int = 0, rows: int = 128, s: int = 16384,
+            n_docs: int = 65536, doc_len: int = 1023, n_templates: int = 512,
+            t_len: int = 512, vocab: int = 128256, steps: int = 32) -> dict:
+    """Config 5 (multi-GPU global drafter): a corpus of n_docs template
+    documents whose tokens and SEPs fill 2^26 positions, the same on every
+    rank (shared seed), and this rank's query rows (rows x s, built the
+    same way from new draws) with its decode-step samples."""
+    rng = np.random.default_rng(seed)
+    z = Zipf(1.1, vocab)
+    templates = z.draw(rng, (n_templates, t_len))
+    corpus_docs = template_docs(rng, n_docs, doc_len, templates, z)
+    rr = np.random.default_rng(seed * 1000 + 17 + rank)
+    toks = template_docs(rr, rows, s, templates, z)
+    q = rr.integers(s // 2, s - 8 * steps, size=rows).astype(np.int32)
+    sampled = np.stack([sampled_tokens(rr, rows, 5, z) for _ in range(steps)])
+    return {"corpus_docs": corpus_docs, "token_ids": toks, "num_tokens": q,
+            "sampled": sampled}
