@@ -20,6 +20,13 @@
 // per-digit scan over tiles, and a stable scatter that ranks each 32-key
 // warp round with 8 ballots (no __match_any_sync, which is slow on
 // sm_100a).
+// Segmented rounds: the active list is in SA order, so it is already
+// grouped; a round only has to order each group by its second key. Groups
+// of at most kSegHalo suffixes (on copy-heavy text nearly all of them:
+// 10 M of 16 M suffixes stay active for 8 rounds, in groups of a few) are
+// ranked in shared memory by the block whose tile holds their head, in one
+// pass; only the suffixes of larger groups are compacted, radix-sorted by
+// (group, second key) and scattered back into their groups' slots.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -378,6 +385,211 @@ __global__ void __launch_bounds__(kScanThreads)
 }
 
 // ---------------------------------------------------------------------------
+// segmented rounds
+// ---------------------------------------------------------------------------
+constexpr int kSegThreads = 256;
+constexpr int kSegTile = 2048;   // active-list elements owned by a block
+constexpr int kSegHalo = 256;    // largest group ranked on chip
+constexpr int kSegItems = 11;    // window elements per thread
+constexpr int kSegWin = kSegTile + 2 * kSegHalo + 2;  // (+ one each side)
+static_assert(kSegThreads * kSegItems >= kSegWin, "window does not fit");
+
+// Exclusive prefix max / suffix min over the threads of a block (one value
+// per thread; Hillis-Steele in shared memory).
+__device__ __forceinline__ int block_excl_prefix_max(int v, int* buf) {
+  const int t = threadIdx.x;
+  buf[t] = v;
+  __syncthreads();
+  for (int o = 1; o < kSegThreads; o <<= 1) {
+    const int x = t >= o ? buf[t - o] : INT32_MIN;
+    __syncthreads();
+    if (t >= o) buf[t] = max(buf[t], x);
+    __syncthreads();
+  }
+  const int r = t > 0 ? buf[t - 1] : INT32_MIN;
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ int block_excl_suffix_min(int v, int* buf) {
+  const int t = threadIdx.x;
+  buf[t] = v;
+  __syncthreads();
+  for (int o = 1; o < kSegThreads; o <<= 1) {
+    const int x = t + o < kSegThreads ? buf[t + o] : INT32_MAX;
+    __syncthreads();
+    if (t + o < kSegThreads) buf[t] = min(buf[t], x);
+    __syncthreads();
+  }
+  const int r = t + 1 < kSegThreads ? buf[t + 1] : INT32_MAX;
+  __syncthreads();
+  return r;
+}
+
+// Element w of the window is element x = t0 - kSegHalo - 1 + w of the
+// active list (sentinel groups outside the list). A block owns x in
+// [t0, t0 + kSegTile): it flags each owned element that belongs to a large
+// group (for the global path) and writes every element of the small groups
+// whose head it owns, in (second key, list position) order, at the group's
+// slots. A small group's members all lie within kSegHalo of its head, so
+// the window holds every group that the block must see whole.
+__global__ void __launch_bounds__(kSegThreads)
+    seg_local_kernel(const uint64_t* __restrict__ K,
+                     const uint32_t* __restrict__ V, int64_t m, int sb,
+                     uint64_t* __restrict__ Kout, uint32_t* __restrict__ Vout,
+                     uint8_t* __restrict__ large) {
+  extern __shared__ __align__(16) unsigned char seg_smem[];
+  uint64_t* sk = reinterpret_cast<uint64_t*>(seg_smem);   // [kSegWin]
+  int* first = reinterpret_cast<int*>(sk + kSegWin);      // [kSegWin]
+  int* last = first + kSegWin;                            // [kSegWin]
+  __shared__ int sbuf[kSegThreads];
+  const int t = threadIdx.x;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kSegTile;
+  const int64_t wbase = t0 - kSegHalo - 1;
+  const uint64_t kmask = (uint64_t(1) << sb) - 1;
+  // group ids of real keys are < 2^31 <= 2^(63 - sb); the two sentinels
+  // (before / after the list) have distinct larger ids
+  const uint64_t before_key = uint64_t(1) << 63;
+  const uint64_t after_key = (uint64_t(3) << 62);
+  for (int w = t; w < kSegWin; w += kSegThreads) {
+    const int64_t x = wbase + w;
+    sk[w] = (x >= 0 && x < m) ? K[x] : (x < 0 ? before_key : after_key);
+  }
+  __syncthreads();
+  // first[w]: head of w's group (<= 0: at or before the window start);
+  // last[w]: its last element (>= kSegWin - 1: at or after the window end)
+  const int w0 = t * kSegItems;
+  int run = INT32_MIN;
+#pragma unroll
+  for (int q = 0; q < kSegItems; ++q) {
+    const int w = w0 + q;
+    if (w < kSegWin) {
+      if (w > 0 && (sk[w] >> sb) != (sk[w - 1] >> sb)) run = w;
+      first[w] = run;
+    }
+  }
+  const int pre = block_excl_prefix_max(run, sbuf);
+#pragma unroll
+  for (int q = 0; q < kSegItems; ++q) {
+    const int w = w0 + q;
+    if (w < kSegWin) {
+      const int f = max(first[w], pre);
+      first[w] = f < 0 ? 0 : f;
+    }
+  }
+  int rrun = INT32_MAX;
+#pragma unroll
+  for (int q = kSegItems - 1; q >= 0; --q) {
+    const int w = w0 + q;
+    if (w < kSegWin) {
+      if (w < kSegWin - 1 && (sk[w] >> sb) != (sk[w + 1] >> sb)) rrun = w;
+      last[w] = rrun;
+    }
+  }
+  const int suf = block_excl_suffix_min(rrun, sbuf);
+#pragma unroll
+  for (int q = 0; q < kSegItems; ++q) {
+    const int w = w0 + q;
+    if (w < kSegWin) {
+      const int l = min(last[w], suf);
+      last[w] = l > kSegWin - 1 ? kSegWin - 1 : l;
+    }
+  }
+  __syncthreads();
+  // owned elements and the forward halo
+  const int own0 = kSegHalo + 1, own1 = own0 + kSegTile;
+  for (int w = own0 + t; w < kSegWin - 1; w += kSegThreads) {
+    const int64_t x = wbase + w;
+    if (x >= m) break;
+    const int f = first[w], l = last[w];
+    const bool small = f > 0 && l < kSegWin - 1 && l - f + 1 <= kSegHalo;
+    if (w < own1) large[x] = small ? 0 : 1;
+    if (!small || f < own0 || f >= own1) continue;  // another block's group
+    const uint64_t kw = sk[w] & kmask;
+    int rank = 0;
+    for (int u = f; u <= l; ++u) {
+      const uint64_t ku = sk[u] & kmask;
+      rank += (ku < kw) || (ku == kw && u < w);
+    }
+    const int64_t pos = wbase + f + rank;
+    Kout[pos] = sk[w];
+    Vout[pos] = V[x];
+  }
+}
+
+// Per scan block: number of flagged elements (blk_max zeroed so that the
+// shared scan kernel can be reused).
+__global__ void __launch_bounds__(kScanThreads)
+    flag_count_kernel(const uint8_t* __restrict__ flag, int64_t m,
+                      uint32_t* __restrict__ blk_max,
+                      uint32_t* __restrict__ blk_sum) {
+  __shared__ uint32_t ss[kSortWarps];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanBlock;
+  uint32_t sum = 0;
+  for (int r = 0; r < kScanItems; ++r) {
+    const int64_t t = base + r * kScanThreads + threadIdx.x;
+    if (t < m) sum += flag[t];
+  }
+  sum = __reduce_add_sync(SG_FULL_MASK, sum);
+  if (lane_id() == 0) ss[warp_id()] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t b = 0;
+    for (int w = 0; w < kSortWarps; ++w) b += ss[w];
+    blk_max[blockIdx.x] = 0;
+    blk_sum[blockIdx.x] = b;
+  }
+}
+
+// Flagged elements in order: LK[u] = K[t], LV[u] = V[t], LT[u] = t.
+__global__ void __launch_bounds__(kScanThreads)
+    flag_compact_kernel(const uint8_t* __restrict__ flag,
+                        const uint64_t* __restrict__ K,
+                        const uint32_t* __restrict__ V, int64_t m,
+                        const uint32_t* __restrict__ blk_sum,
+                        uint64_t* __restrict__ LK, uint32_t* __restrict__ LV,
+                        uint32_t* __restrict__ LT) {
+  __shared__ uint32_t ws[kSortWarps];
+  const int lane = lane_id(), warp = warp_id();
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanBlock;
+  uint32_t carry = blk_sum[blockIdx.x];
+  for (int r = 0; r < kScanItems; ++r) {
+    const int64_t t = base + r * kScanThreads + threadIdx.x;
+    const bool f = t < m && flag[t];
+    const unsigned bal = __ballot_sync(SG_FULL_MASK, f);
+    if (lane == 0) ws[warp] = __popc(bal);
+    __syncthreads();
+    uint32_t pre = carry, tot = carry;
+    for (int w = 0; w < kSortWarps; ++w) {
+      if (w < warp) pre += ws[w];
+      tot += ws[w];
+    }
+    if (f) {
+      const uint32_t u = pre + __popc(bal & ((1u << lane) - 1u));
+      LK[u] = K[t];
+      LV[u] = V[t];
+      LT[u] = static_cast<uint32_t>(t);
+    }
+    carry = tot;
+    __syncthreads();
+  }
+}
+
+// Sorted large-group elements back to their slots.
+__global__ void flag_scatter_kernel(const uint64_t* __restrict__ SK,
+                                    const uint32_t* __restrict__ SV,
+                                    const uint32_t* __restrict__ LT,
+                                    int64_t ml, uint64_t* __restrict__ Kout,
+                                    uint32_t* __restrict__ Vout) {
+  const int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (u < ml) {
+    const uint32_t pos = LT[u];
+    Kout[pos] = SK[u];
+    Vout[pos] = SV[u];
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host driver
 // ---------------------------------------------------------------------------
 static int bitlen(uint64_t x) {
@@ -394,6 +606,10 @@ struct SaWorkspace {
   uint32_t* V[2];
   uint32_t* rank;
   uint32_t* act[2];
+  uint64_t* LK;      // large-group elements: keys, values, list positions
+  uint32_t* LV;
+  uint32_t* LT;
+  uint8_t* flag;     // element of a large group
   uint32_t* tile_hist;
   uint32_t* totals;
   uint32_t* blk_max;
@@ -423,6 +639,10 @@ static SaWorkspace carve(void* base, int64_t n) {
   w.rank = reinterpret_cast<uint32_t*>(take(4 * un));
   w.act[0] = reinterpret_cast<uint32_t*>(take(4 * un));
   w.act[1] = reinterpret_cast<uint32_t*>(take(4 * un));
+  w.LK = reinterpret_cast<uint64_t*>(take(8 * un));
+  w.LV = reinterpret_cast<uint32_t*>(take(4 * un));
+  w.LT = reinterpret_cast<uint32_t*>(take(4 * un));
+  w.flag = reinterpret_cast<uint8_t*>(take(un));
   w.tile_hist = reinterpret_cast<uint32_t*>(take(4 * 256 * ntiles));
   w.totals = reinterpret_cast<uint32_t*>(take(4 * 256));
   w.blk_max = reinterpret_cast<uint32_t*>(take(4 * nblk));
@@ -432,23 +652,70 @@ static SaWorkspace carve(void* base, int64_t n) {
   return w;
 }
 
-// Stable LSD sort of (K[cur], V[cur]) by the low `bits` bits; returns the
-// buffer index holding the result.
-static int radix_sort(SaWorkspace& w, int cur, int64_t m, int bits,
-                      cudaStream_t st) {
+// Stable LSD sort of (kb[cur], vb[cur]) by the low `bits` bits, ping-
+// ponging between the two buffer pairs; returns the index holding the
+// result.
+static int radix_sort_pair(SaWorkspace& w, uint64_t* const kb[2],
+                           uint32_t* const vb[2], int cur, int64_t m,
+                           int bits, cudaStream_t st) {
   const int ntiles = static_cast<int>((m + kTile - 1) / kTile);
   for (int shift = 0; shift < bits; shift += 8) {
     zero_u32_kernel<<<1, 256, 0, st>>>(w.totals, 256);
     rs_hist_kernel<<<ntiles, kSortThreads, 0, st>>>(
-        w.K[cur], m, shift, w.tile_hist, ntiles, w.totals);
+        kb[cur], m, shift, w.tile_hist, ntiles, w.totals);
     rs_scan_kernel<<<256, kSortThreads, 0, st>>>(w.tile_hist, ntiles,
                                                  w.totals);
     rs_scatter_kernel<<<ntiles, kSortThreads, 0, st>>>(
-        w.K[cur], w.V[cur], w.K[1 - cur], w.V[1 - cur], m, shift,
-        w.tile_hist, ntiles);
+        kb[cur], vb[cur], kb[1 - cur], vb[1 - cur], m, shift, w.tile_hist,
+        ntiles);
     cur = 1 - cur;
   }
   return cur;
+}
+
+static int radix_sort(SaWorkspace& w, int cur, int64_t m, int bits,
+                      cudaStream_t st) {
+  return radix_sort_pair(w, w.K, w.V, cur, m, bits, st);
+}
+
+// Reads a device count into *out (host sync).
+static int read_count(const int64_t* dev, int64_t* out, cudaStream_t st) {
+  cudaError_t e = cudaMemcpyAsync(out, dev, sizeof(int64_t),
+                                  cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return SG_ERR_CUDA;
+  }
+  return SG_OK;
+}
+
+// Orders the active list (K[0], V[0]; m elements, grouped) by
+// (group, second key) into (K[1], V[1]): small groups on chip, large ones
+// through the global radix sort.
+static int segmented_sort(SaWorkspace& w, int64_t m, int sb, int bits,
+                          cudaStream_t st) {
+  const int nseg = static_cast<int>((m + kSegTile - 1) / kSegTile);
+  const size_t seg_smem = static_cast<size_t>(kSegWin) * 16;
+  seg_local_kernel<<<nseg, kSegThreads, seg_smem, st>>>(
+      w.K[0], w.V[0], m, sb, w.K[1], w.V[1], w.flag);
+  const int nblk = static_cast<int>((m + kScanBlock - 1) / kScanBlock);
+  flag_count_kernel<<<nblk, kScanThreads, 0, st>>>(w.flag, m, w.blk_max,
+                                                   w.blk_sum);
+  round_scan_blocks_kernel<<<1, 1024, 0, st>>>(w.blk_max, w.blk_sum, nblk,
+                                               w.m_dev);
+  int64_t ml = 0;
+  const int rc = read_count(w.m_dev, &ml, st);
+  if (rc != SG_OK) return rc;
+  if (ml == 0) return SG_OK;
+  flag_compact_kernel<<<nblk, kScanThreads, 0, st>>>(
+      w.flag, w.K[0], w.V[0], m, w.blk_sum, w.LK, w.LV, w.LT);
+  uint64_t* const kb[2] = {w.LK, w.K[0]};
+  uint32_t* const vb[2] = {w.LV, w.V[0]};
+  const int c = radix_sort_pair(w, kb, vb, 0, ml, bits, st);
+  flag_scatter_kernel<<<static_cast<unsigned>((ml + 255) / 256), 256, 0,
+                        st>>>(kb[c], vb[c], w.LT, ml, w.K[1], w.V[1]);
+  return SG_OK;
 }
 
 // One apply pass; returns the next active count (host sync).
@@ -521,7 +788,9 @@ extern "C" int sg_build_suffix_array(const int32_t* tokens, int64_t n,
     if (h >= n) return SG_ERR_CUDA;  // cannot happen for a correct build
     make_keys_kernel<<<static_cast<unsigned>((m + 255) / 256), 256, 0, st>>>(
         w.act[acur], sa_out, w.rank, n, m, h, sb, w.K[0], w.V[0]);
-    kcur = radix_sort(w, 0, m, pb + sb, st);
+    const int rc = segmented_sort(w, m, sb, pb + sb, st);
+    if (rc != SG_OK) return rc;
+    kcur = 1;
     int64_t m_next = 0;
     if (!apply_round(w, kcur, w.act[acur], w.act[1 - acur], m, sa_out, st,
                      &m_next, &err))
