@@ -10,7 +10,7 @@ from collections.abc import Sequence
 import torch
 
 from suffixgpu_b200._lib import (DraftParams, LocalInputs, LocalOutputs,
-                                 call, ptr, stream_of)
+                                 check, lib, ptr)
 from suffixgpu_b200.ops import as_i32, require_cuda
 
 
@@ -46,6 +46,14 @@ class LocalMatchKernel:
         self.support_thresholds = tuple(int(t) for t in support_thresholds)
         self.num_backoff = _check_thresholds(self.support_thresholds)
         self._pcache: dict = {}
+        # per-call host work kept small: the argument structs are reused
+        # (one host thread drives a drafter) and the entry point is bound
+        # once
+        self._ins = LocalInputs()
+        self._outs = LocalOutputs()
+        self._ins_ref = ctypes.byref(self._ins)
+        self._outs_ref = ctypes.byref(self._outs)
+        self._fn = None
 
     def to(self, device) -> "LocalMatchKernel":
         return self
@@ -73,7 +81,8 @@ class LocalMatchKernel:
             valid_count: torch.Tensor | None = None,
             mask: torch.Tensor | None = None, limit: int | None = None,
             extras: bool = False) -> dict:
-        """One fused launch; returns a dict of output tensors."""
+        """One fused launch; returns a dict of newly allocated output
+        tensors (the int32 ones are views of one allocation)."""
         dev = require_cuda(num_tokens, token_ids)
         if token_ids.dtype != torch.int32 or token_ids.dim() != 2 \
                 or token_ids.stride(1) != 1:
@@ -82,36 +91,47 @@ class LocalMatchKernel:
         b, s = token_ids.shape
         k = self.k
         n = as_i32(num_tokens)
-        out = {"draft": torch.empty(b, k, dtype=torch.int32, device=dev),
-               "num_valid": torch.empty(b, dtype=torch.int32, device=dev)}
-        ins = LocalInputs()
-        ins.num_tokens = ptr(n)
-        ins.token_ids = ptr(token_ids)
+        ins, outs = self._ins, self._outs
+        ins.num_tokens = n.data_ptr()
+        ins.token_ids = token_ids.data_ptr()
         ins.limit = s if limit is None else int(limit)
+        ins.sampled = None
+        ins.sampled_cols = 0
+        ins.valid_count = None
+        ins.mask = None
+        # draft [b, k], num_valid [b], new_counts [b] (+ best_len, best_occ)
+        n_i32 = b * (k + 2 + (2 if extras else 0))
+        buf = torch.empty(n_i32, dtype=torch.int32, device=dev)
+        out = {"draft": buf[:b * k].view(b, k),
+               "num_valid": buf[b * k:b * (k + 1)]}
         if sampled is not None:
             sampled = as_i32(sampled)
-            ins.sampled = ptr(sampled)
+            ins.sampled = sampled.data_ptr()
             ins.sampled_cols = sampled.shape[1]
             if valid_count is not None:
                 valid_count = as_i32(valid_count)
-                ins.valid_count = ptr(valid_count)
-            out["new_counts"] = torch.empty(b, dtype=torch.int32, device=dev)
+                ins.valid_count = valid_count.data_ptr()
+            out["new_counts"] = buf[b * (k + 1):b * (k + 2)]
         elif mask is not None:
             mask = mask.to(torch.bool).contiguous()
-            ins.mask = ptr(mask)
+            ins.mask = mask.data_ptr()
         if extras:
+            out["best_len"] = buf[b * (k + 2):b * (k + 3)]
+            out["best_occ"] = buf[b * (k + 3):b * (k + 4)]
             out["best_score"] = torch.empty(b, dtype=torch.float32,
                                             device=dev)
-            out["best_len"] = torch.empty(b, dtype=torch.int32, device=dev)
-            out["best_occ"] = torch.empty(b, dtype=torch.int32, device=dev)
             out["row_mask"] = torch.empty(b, dtype=torch.bool, device=dev)
-        outs = LocalOutputs()
         for name in ("draft", "num_valid", "new_counts", "best_score",
                      "best_len", "best_occ", "row_mask"):
             setattr(outs, name, ptr(out.get(name)))
         p = self.params(b, s, token_ids.stride(0))
-        call("sg_local_draft", ctypes.byref(p), ctypes.byref(ins),
-             ctypes.byref(outs), stream_of(dev))
+        fn = self._fn
+        if fn is None:
+            fn = self._fn = lib().sg_local_draft
+        st = fn(ctypes.byref(p), self._ins_ref, self._outs_ref,
+                torch.cuda.current_stream(dev).cuda_stream)
+        if st != 0:
+            check("sg_local_draft", st)
         return out
 
     def forward(self, num_tokens_no_spec: torch.Tensor,
