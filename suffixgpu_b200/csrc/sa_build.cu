@@ -772,7 +772,7 @@ extern "C" int sg_build_suffix_array(const int32_t* tokens, int64_t n,
     return SG_ERR_WORKSPACE;
   SaWorkspace w = carve(workspace, n);
 
-  // round 0: sort by the first token
+  // initial pass: sort by the first token
   init_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(
       tokens, n, w.K[0], w.V[0]);
   int kcur = radix_sort(w, 0, n, 32, st);

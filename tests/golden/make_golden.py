@@ -1,11 +1,11 @@
 """Generate the golden vectors that pin the oracle (and the CUDA path).
 
 Runs the reference project's own pure-PyTorch CPU path (zip95297/SuffixGPU,
-imported from a local checkout given by --ref, default /root/reference) on
-seeded inputs and writes compressed ``.npz`` fixtures next to this file.
-The reference is never needed at test time: the fixtures are committed.
+imported from the local checkout given by --ref) on seeded inputs and
+writes compressed ``.npz`` fixtures next to this file. The reference is
+never needed at test time: the fixtures are committed.
 
-Usage: python tests/golden/make_golden.py [--ref PATH]
+Usage: python tests/golden/make_golden.py --ref PATH_TO_REFERENCE_CHECKOUT
 """
 
 from __future__ import annotations
@@ -163,7 +163,8 @@ def global_cases(torch, Drafter) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True,
+                    help="checkout of the reference project")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     import torch
