@@ -10,7 +10,7 @@ from collections.abc import Sequence
 import torch
 
 from suffixgpu_b200._lib import (DraftParams, LocalInputs, LocalOutputs,
-                                 check, lib, ptr)
+                                 check, lib, stream_of)
 from suffixgpu_b200.ops import as_i32, require_cuda
 
 
@@ -83,14 +83,18 @@ class LocalMatchKernel:
             extras: bool = False) -> dict:
         """One fused launch; returns a dict of newly allocated output
         tensors (the int32 ones are views of one allocation)."""
-        dev = require_cuda(num_tokens, token_ids)
+        if not (token_ids.is_cuda and num_tokens.is_cuda):
+            require_cuda(num_tokens, token_ids)
+        dev = token_ids.device
         if token_ids.dtype != torch.int32 or token_ids.dim() != 2 \
                 or token_ids.stride(1) != 1:
             raise ValueError("token_ids must be an int32 [B, S] tensor with "
                              "unit column stride")
         b, s = token_ids.shape
         k = self.k
-        n = as_i32(num_tokens)
+        n = num_tokens
+        if n.dtype != torch.int32 or not n.is_contiguous():
+            n = as_i32(n)
         ins, outs = self._ins, self._outs
         ins.num_tokens = n.data_ptr()
         ins.token_ids = token_ids.data_ptr()
@@ -99,37 +103,49 @@ class LocalMatchKernel:
         ins.sampled_cols = 0
         ins.valid_count = None
         ins.mask = None
-        # draft [b, k], num_valid [b], new_counts [b] (+ best_len, best_occ)
+        # one int32 allocation: draft [b, k], num_valid [b], new_counts [b]
+        # (+ best_len, best_occ); their addresses follow from its base
         n_i32 = b * (k + 2 + (2 if extras else 0))
         buf = torch.empty(n_i32, dtype=torch.int32, device=dev)
+        base = buf.data_ptr()
         out = {"draft": buf[:b * k].view(b, k),
                "num_valid": buf[b * k:b * (k + 1)]}
+        outs.draft = base
+        outs.num_valid = base + 4 * b * k
+        outs.new_counts = None
+        outs.best_score = None
+        outs.best_len = None
+        outs.best_occ = None
+        outs.row_mask = None
         if sampled is not None:
-            sampled = as_i32(sampled)
+            if sampled.dtype != torch.int32 or not sampled.is_contiguous():
+                sampled = as_i32(sampled)
             ins.sampled = sampled.data_ptr()
             ins.sampled_cols = sampled.shape[1]
             if valid_count is not None:
                 valid_count = as_i32(valid_count)
                 ins.valid_count = valid_count.data_ptr()
             out["new_counts"] = buf[b * (k + 1):b * (k + 2)]
+            outs.new_counts = base + 4 * b * (k + 1)
         elif mask is not None:
             mask = mask.to(torch.bool).contiguous()
             ins.mask = mask.data_ptr()
         if extras:
             out["best_len"] = buf[b * (k + 2):b * (k + 3)]
             out["best_occ"] = buf[b * (k + 3):b * (k + 4)]
+            outs.best_len = base + 4 * b * (k + 2)
+            outs.best_occ = base + 4 * b * (k + 3)
             out["best_score"] = torch.empty(b, dtype=torch.float32,
                                             device=dev)
             out["row_mask"] = torch.empty(b, dtype=torch.bool, device=dev)
-        for name in ("draft", "num_valid", "new_counts", "best_score",
-                     "best_len", "best_occ", "row_mask"):
-            setattr(outs, name, ptr(out.get(name)))
+            outs.best_score = out["best_score"].data_ptr()
+            outs.row_mask = out["row_mask"].data_ptr()
         p = self.params(b, s, token_ids.stride(0))
         fn = self._fn
         if fn is None:
             fn = self._fn = lib().sg_local_draft
         st = fn(ctypes.byref(p), self._ins_ref, self._outs_ref,
-                torch.cuda.current_stream(dev).cuda_stream)
+                stream_of(dev))
         if st != 0:
             check("sg_local_draft", st)
         return out
