@@ -150,6 +150,25 @@ def register(name: str, argtypes: list, restype=c_int) -> None:
         fn.argtypes = argtypes
 
 
+_ops = None
+
+
+def torch_ops():
+    """The torch operators of libsuffixgpu_b200_torch.so (loaded once;
+    raises if it has not been built)."""
+    global _ops
+    if _ops is None:
+        path = os.path.join(os.path.dirname(os.path.abspath(__file__)),
+                            "libsuffixgpu_b200_torch.so")
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} is missing: run python -m "
+                               "suffixgpu_b200.build")
+        lib()  # the kernel library first (the operator links to it)
+        torch.ops.load_library(path)
+        _ops = torch.ops.suffixgpu_b200
+    return _ops
+
+
 def call(name: str, *args) -> None:
     """Call an entry point; raise on a non-zero status."""
     check(name, getattr(lib(), name)(*args))

@@ -4,7 +4,11 @@
 ``sm_100a`` (``-gencode arch=compute_100a,code=sm_100a``) into
 ``suffixgpu_b200/libsuffixgpu_b200.so``. Objects are rebuilt only when a
 source or header is newer. The library has no torch dependency: it exports
-the C ABI declared in ``include/suffixgpu.h``.
+the C ABI declared in ``include/suffixgpu.h``. ``csrc/torch_ops.cpp`` (the
+torch operator over that ABI for the per-step call) is compiled with the
+host C++ compiler against torch's headers into
+``suffixgpu_b200/libsuffixgpu_b200_torch.so``, linked to the kernel
+library.
 """
 
 from __future__ import annotations
@@ -21,6 +25,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OBJ = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libsuffixgpu_b200.so")
+TORCH_LIB = os.path.join(PKG, "libsuffixgpu_b200_torch.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
@@ -73,7 +78,37 @@ def build(verbose: bool = False, extra_flags: list[str] | None = None) -> str:
     if jobs or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(
             os.path.getmtime(o) for o in objs):
         run([nvcc, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"])
+    build_torch_ops(verbose)
     return LIB
+
+
+def build_torch_ops(verbose: bool = False) -> str:
+    """Compile the torch operator (incrementally) against torch's headers
+    and libraries, linked to the kernel library (found next to it)."""
+    src = os.path.join(CSRC, "torch_ops.cpp")
+    newest = max(os.path.getmtime(src), os.path.getmtime(LIB),
+                 os.path.getmtime(os.path.join(ROOT, "include", "suffixgpu.h")))
+    if os.path.exists(TORCH_LIB) and os.path.getmtime(TORCH_LIB) >= newest:
+        return TORCH_LIB
+    import torch
+    import torch.utils.cpp_extension as ce
+    cxx = os.environ.get("CXX") or shutil.which("g++") or "g++"
+    cuda_inc = os.path.join(os.path.dirname(os.path.dirname(_nvcc())),
+                            "include")
+    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared",
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
+           src, "-o", TORCH_LIB, "-I" + cuda_inc]
+    cmd += ["-I" + p for p in ce.include_paths(device_type="cuda")]
+    cmd += ["-L" + p for p in ce.library_paths(device_type="cuda")]
+    cmd += ["-L" + PKG, "-lsuffixgpu_b200", "-Wl,-rpath,$ORIGIN",
+            "-lc10", "-ltorch", "-ltorch_cpu", "-lc10_cuda", "-ltorch_cuda"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"torch op build failed:\n{' '.join(cmd)}\n"
+                           f"{r.stderr}")
+    return TORCH_LIB
 
 
 if __name__ == "__main__":

@@ -1,0 +1,114 @@
+// torch operator over the C ABI for the per-step drafter call.
+//
+// suffixgpu_b200::local_draft wraps sg_local_draft (the fused local step of
+// SuffixGPUDrafter.propose_with_update / propose, proposer.py:186-331) so
+// that the eager Python call costs one dispatcher hop: the outputs are
+// allocated here (one int32 buffer and views) and the launch goes to the
+// current torch stream. The drafter's settings arrive as a small host
+// tensor holding an sg_draft_params struct; the batch shape comes from
+// token_ids. Errors raise (TORCH_CHECK) with the library's status string.
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/library.h>
+
+#include <cstring>
+#include <vector>
+
+#include "../../include/suffixgpu.h"
+
+namespace {
+
+std::vector<at::Tensor> local_draft(const at::Tensor& num_tokens,
+                                    const at::Tensor& token_ids,
+                                    const c10::optional<at::Tensor>& sampled,
+                                    const c10::optional<at::Tensor>& valid_count,
+                                    const c10::optional<at::Tensor>& mask,
+                                    const at::Tensor& params, int64_t limit,
+                                    bool extras) {
+  TORCH_CHECK(token_ids.is_cuda() && num_tokens.is_cuda(),
+              "suffixgpu_b200 ops need CUDA tensors");
+  TORCH_CHECK(token_ids.scalar_type() == at::kInt && token_ids.dim() == 2 &&
+                  token_ids.stride(1) == 1,
+              "token_ids must be an int32 [B, S] tensor with unit column stride");
+  TORCH_CHECK(params.device().is_cpu() &&
+                  params.nbytes() == sizeof(sg_draft_params),
+              "params must hold one sg_draft_params struct");
+  const c10::cuda::CUDAGuard guard(token_ids.device());
+  const int64_t b = token_ids.size(0), s = token_ids.size(1);
+  sg_draft_params p;
+  std::memcpy(&p, params.data_ptr(), sizeof(p));
+  p.batch = static_cast<int32_t>(b);
+  p.seq_len = static_cast<int32_t>(s);
+  p.row_stride = token_ids.stride(0);
+  const int64_t k = p.k;
+  at::Tensor n = num_tokens;
+  if (n.scalar_type() != at::kInt || !n.is_contiguous())
+    n = n.to(at::kInt).contiguous();
+  sg_local_inputs in{};
+  in.num_tokens = n.data_ptr<int32_t>();
+  in.token_ids = token_ids.data_ptr<int32_t>();
+  in.limit = limit;
+  const int64_t n_i32 = b * (k + 2 + (extras ? 2 : 0));
+  at::Tensor buf = at::empty({n_i32}, token_ids.options());
+  int32_t* base = buf.data_ptr<int32_t>();
+  sg_local_outputs out{};
+  out.draft = base;
+  out.num_valid = base + b * k;
+  std::vector<at::Tensor> res;
+  res.reserve(7);
+  res.push_back(buf.narrow(0, 0, b * k).view({b, k}));
+  res.push_back(buf.narrow(0, b * k, b));
+  at::Tensor samp, vc, msk;
+  if (sampled.has_value()) {
+    samp = *sampled;
+    if (samp.scalar_type() != at::kInt || !samp.is_contiguous())
+      samp = samp.to(at::kInt).contiguous();
+    in.sampled = samp.data_ptr<int32_t>();
+    in.sampled_cols = static_cast<int32_t>(samp.size(1));
+    if (valid_count.has_value()) {
+      vc = valid_count->to(at::kInt).contiguous();
+      in.valid_count = vc.data_ptr<int32_t>();
+    }
+    out.new_counts = base + b * (k + 1);
+    res.push_back(buf.narrow(0, b * (k + 1), b));
+  } else {
+    res.push_back(buf.narrow(0, 0, 0));  // no update: empty new_counts
+    if (mask.has_value()) {
+      msk = mask->to(at::kBool).contiguous();
+      in.mask = reinterpret_cast<const uint8_t*>(msk.data_ptr<bool>());
+    }
+  }
+  if (extras) {
+    at::Tensor score = at::empty({b}, token_ids.options().dtype(at::kFloat));
+    at::Tensor rmask = at::empty({b}, token_ids.options().dtype(at::kBool));
+    out.best_len = base + b * (k + 2);
+    out.best_occ = base + b * (k + 3);
+    out.best_score = score.data_ptr<float>();
+    out.row_mask = reinterpret_cast<uint8_t*>(rmask.data_ptr<bool>());
+    res.push_back(score);
+    res.push_back(buf.narrow(0, b * (k + 2), b));
+    res.push_back(buf.narrow(0, b * (k + 3), b));
+    res.push_back(rmask);
+  }
+  const int st = sg_local_draft(
+      &p, &in, &out,
+      reinterpret_cast<sg_stream_t>(
+          c10::cuda::getCurrentCUDAStream(token_ids.device().index()).stream()));
+  TORCH_CHECK(st == SG_OK, "sg_local_draft failed: ", sg_status_string(st),
+              " (status ", st, ", cuda error ", sg_last_cuda_error(), ")");
+  return res;
+}
+
+}  // namespace
+
+TORCH_LIBRARY(suffixgpu_b200, m) {
+  m.def(
+      "local_draft(Tensor num_tokens, Tensor token_ids, Tensor? sampled, "
+      "Tensor? valid_count, Tensor? mask, Tensor params, int limit, "
+      "bool extras) -> Tensor[]");
+}
+
+TORCH_LIBRARY_IMPL(suffixgpu_b200, CUDA, m) {
+  m.impl("local_draft", &local_draft);
+}

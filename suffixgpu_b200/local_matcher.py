@@ -4,14 +4,12 @@ the fused sm_100a kernel ``sg_local_draft``."""
 
 from __future__ import annotations
 
-import ctypes
 from collections.abc import Sequence
 
 import torch
 
-from suffixgpu_b200._lib import (DraftParams, LocalInputs, LocalOutputs,
-                                 check, lib, stream_of)
-from suffixgpu_b200.ops import as_i32, require_cuda
+from suffixgpu_b200._lib import DraftParams, torch_ops
+from suffixgpu_b200.ops import require_cuda
 
 
 def _check_thresholds(support_thresholds: Sequence[int]) -> int:
@@ -46,14 +44,8 @@ class LocalMatchKernel:
         self.support_thresholds = tuple(int(t) for t in support_thresholds)
         self.num_backoff = _check_thresholds(self.support_thresholds)
         self._pcache: dict = {}
-        # per-call host work kept small: the argument structs are reused
-        # (one host thread drives a drafter) and the entry point is bound
-        # once
-        self._ins = LocalInputs()
-        self._outs = LocalOutputs()
-        self._ins_ref = ctypes.byref(self._ins)
-        self._outs_ref = ctypes.byref(self._outs)
-        self._fn = None
+        self._op = None
+        self._params_t: torch.Tensor | None = None
 
     def to(self, device) -> "LocalMatchKernel":
         return self
@@ -81,73 +73,28 @@ class LocalMatchKernel:
             valid_count: torch.Tensor | None = None,
             mask: torch.Tensor | None = None, limit: int | None = None,
             extras: bool = False) -> dict:
-        """One fused launch; returns a dict of newly allocated output
-        tensors (the int32 ones are views of one allocation)."""
+        """One fused launch (the torch operator over sg_local_draft);
+        returns a dict of newly allocated output tensors."""
         if not (token_ids.is_cuda and num_tokens.is_cuda):
             require_cuda(num_tokens, token_ids)
-        dev = token_ids.device
-        if token_ids.dtype != torch.int32 or token_ids.dim() != 2 \
-                or token_ids.stride(1) != 1:
-            raise ValueError("token_ids must be an int32 [B, S] tensor with "
-                             "unit column stride")
-        b, s = token_ids.shape
-        k = self.k
-        n = num_tokens
-        if n.dtype != torch.int32 or not n.is_contiguous():
-            n = as_i32(n)
-        ins, outs = self._ins, self._outs
-        ins.num_tokens = n.data_ptr()
-        ins.token_ids = token_ids.data_ptr()
-        ins.limit = s if limit is None else int(limit)
-        ins.sampled = None
-        ins.sampled_cols = 0
-        ins.valid_count = None
-        ins.mask = None
-        # one int32 allocation: draft [b, k], num_valid [b], new_counts [b]
-        # (+ best_len, best_occ); their addresses follow from its base
-        n_i32 = b * (k + 2 + (2 if extras else 0))
-        buf = torch.empty(n_i32, dtype=torch.int32, device=dev)
-        base = buf.data_ptr()
-        out = {"draft": buf[:b * k].view(b, k),
-               "num_valid": buf[b * k:b * (k + 1)]}
-        outs.draft = base
-        outs.num_valid = base + 4 * b * k
-        outs.new_counts = None
-        outs.best_score = None
-        outs.best_len = None
-        outs.best_occ = None
-        outs.row_mask = None
+        op = self._op
+        if op is None:
+            op = self._op = torch_ops().local_draft
+            # drafter settings as an sg_draft_params struct (the operator
+            # fills in the batch shape)
+            self._params_t = torch.frombuffer(
+                bytearray(bytes(self.params(0, 1, 1))), dtype=torch.uint8)
+        res = op(num_tokens, token_ids, sampled, valid_count, mask,
+                 self._params_t,
+                 token_ids.shape[1] if limit is None else int(limit), extras)
+        out = {"draft": res[0], "num_valid": res[1]}
         if sampled is not None:
-            if sampled.dtype != torch.int32 or not sampled.is_contiguous():
-                sampled = as_i32(sampled)
-            ins.sampled = sampled.data_ptr()
-            ins.sampled_cols = sampled.shape[1]
-            if valid_count is not None:
-                valid_count = as_i32(valid_count)
-                ins.valid_count = valid_count.data_ptr()
-            out["new_counts"] = buf[b * (k + 1):b * (k + 2)]
-            outs.new_counts = base + 4 * b * (k + 1)
-        elif mask is not None:
-            mask = mask.to(torch.bool).contiguous()
-            ins.mask = mask.data_ptr()
+            out["new_counts"] = res[2]
         if extras:
-            out["best_len"] = buf[b * (k + 2):b * (k + 3)]
-            out["best_occ"] = buf[b * (k + 3):b * (k + 4)]
-            outs.best_len = base + 4 * b * (k + 2)
-            outs.best_occ = base + 4 * b * (k + 3)
-            out["best_score"] = torch.empty(b, dtype=torch.float32,
-                                            device=dev)
-            out["row_mask"] = torch.empty(b, dtype=torch.bool, device=dev)
-            outs.best_score = out["best_score"].data_ptr()
-            outs.row_mask = out["row_mask"].data_ptr()
-        p = self.params(b, s, token_ids.stride(0))
-        fn = self._fn
-        if fn is None:
-            fn = self._fn = lib().sg_local_draft
-        st = fn(ctypes.byref(p), self._ins_ref, self._outs_ref,
-                stream_of(dev))
-        if st != 0:
-            check("sg_local_draft", st)
+            out["best_score"] = res[3]
+            out["best_len"] = res[4]
+            out["best_occ"] = res[5]
+            out["row_mask"] = res[6]
         return out
 
     def forward(self, num_tokens_no_spec: torch.Tensor,
