@@ -75,3 +75,13 @@ def test_invalid_arguments_rejected_without_gpu(libpath):
     assert st == 0  # empty batch: nothing to do
     assert L.sg_expand_chain(None, 1, 0, 4, None, None, 0.0, 0.0, None, None,
                              None, None, None) == 1
+
+
+def test_torch_operator_registers():
+    """The in-tree torch operator library loads (no GPU needed) and
+    registers local_draft with the documented schema."""
+    from suffixgpu_b200 import _lib
+    op = _lib.torch_ops().local_draft
+    schema = str(op.default._schema)
+    assert schema.startswith("suffixgpu_b200::local_draft(Tensor num_tokens")
+    assert "Tensor params" in schema and "-> Tensor[]" in schema
