@@ -126,6 +126,7 @@ class GlobalIndex:
         self.delta = torch.zeros(delta_capacity, dtype=torch.int32,
                                  device=dev)
         self.delta_len_t = torch.zeros((), dtype=torch.int64, device=dev)
+        self._sep1 = torch.full((1,), SEP_TOKEN, dtype=torch.int32, device=dev)
         self.active_len = 0
         self.delta_len = 0
         self.active_doc_lens: deque[int] = deque()
@@ -145,7 +146,20 @@ class GlobalIndex:
     # ------------------------------------------------------------------
     def append_documents(self, docs: list[torch.Tensor]) -> None:
         """Append finished-response token tensors to the delta, each
-        followed by one SEP_TOKEN (recorded doc lengths include it)."""
+        followed by one SEP_TOKEN (recorded doc lengths include it). The
+        device writes of consecutive documents go out as one copy."""
+        pending: list[torch.Tensor] = []
+        start = self.delta_len
+
+        def flush():
+            nonlocal pending, start
+            if pending:
+                blob = torch.cat(pending)
+                self.delta[start:start + blob.numel()].copy_(blob)
+                pending = []
+            self.delta_len_t.fill_(self.delta_len)
+            start = self.delta_len
+
         for doc in docs:
             doc = doc.to(self.device).to(torch.int32).reshape(-1)
             n = doc.shape[0]
@@ -155,12 +169,14 @@ class GlobalIndex:
                 doc = doc[-(self.delta_capacity - 1):]
                 n = doc.shape[0]
             if self.delta_len + n + 1 > self.delta_capacity:
+                flush()
                 self._make_room(n + 1)
-            self.delta[self.delta_len:self.delta_len + n].copy_(doc)
-            self.delta[self.delta_len + n] = SEP_TOKEN
+                start = self.delta_len
+            pending.append(doc)
+            pending.append(self._sep1)
             self.delta_len += n + 1
-            self.delta_len_t.fill_(self.delta_len)
             self.delta_doc_lens.append(n + 1)
+        flush()
         self.maybe_rebuild()
 
     def _make_room(self, needed: int) -> None:
@@ -204,18 +220,22 @@ class GlobalIndex:
             return
         # Evict oldest whole docs until the snapshot fits into capacity.
         keep_start = 0
+        evicted = 0
         for ln in self.active_doc_lens:
             if self.active_len - keep_start + self.delta_len \
                     <= self.capacity:
                 break
             keep_start += ln
+            evicted += 1
         n_active_keep = self.active_len - keep_start
         snap = min(self.delta_len, self.capacity - n_active_keep)
         # Clamp the snapshot to a whole-doc boundary in the delta.
         acc = 0
+        absorbed = 0
         for ln in self.delta_doc_lens:
             if acc + ln <= snap:
                 acc += ln
+                absorbed += 1
             else:
                 break
         snap = acc
@@ -231,20 +251,16 @@ class GlobalIndex:
         if snap > 0:
             dst[n_active_keep:n_new].copy_(self.delta[:snap])
 
-        new_doc_lens: deque[int] = deque()
-        acc = 0
-        for ln in self.active_doc_lens:
-            acc += ln
-            if acc > keep_start:
-                new_doc_lens.append(ln)
-        acc = 0
-        for ln in self.delta_doc_lens:
-            acc += ln
-            if acc <= snap:
-                new_doc_lens.append(ln)
+        # kept active docs (all but the evicted oldest) + absorbed delta docs
+        # (work proportional to the evicted and absorbed docs, not to the
+        # thousands of active ones)
+        new_doc_lens: deque[int] = deque(self.active_doc_lens)
+        for _ in range(evicted):
+            new_doc_lens.popleft()
+        new_doc_lens.extend(self.delta_doc_lens[:absorbed])
 
         # Staging owns a copy of the snapshot; compact it out of the delta.
-        docs_absorbed = self._count_docs_within(snap)
+        docs_absorbed = absorbed
         remaining = self.delta_len - snap
         if remaining > 0:
             self.delta[:remaining] = self.delta[snap:self.delta_len].clone()
@@ -295,16 +311,6 @@ class GlobalIndex:
                 with torch.cuda.stream(torch.cuda.ExternalStream(stream)):
                     self.staging_sa[m:].copy_(self._arange[m:])
                 torch.cuda.ExternalStream(stream).synchronize()
-
-    def _count_docs_within(self, tokens: int) -> int:
-        acc = 0
-        count = 0
-        for ln in self.delta_doc_lens:
-            acc += ln
-            if acc > tokens:
-                break
-            count += 1
-        return count
 
     def _finish_swap(self, n_new: int, new_doc_lens: deque[int]) -> None:
         # In-place copies keep the active tensors' storage (graph safety).
