@@ -678,15 +678,70 @@ static int radix_sort(SaWorkspace& w, int cur, int64_t m, int bits,
   return radix_sort_pair(w, w.K, w.V, cur, m, bits, st);
 }
 
-// Reads a device count into *out (host sync).
-static int read_count(const int64_t* dev, int64_t* out, cudaStream_t st) {
-  cudaError_t e = cudaMemcpyAsync(out, dev, sizeof(int64_t),
+// Host landing slots for the counts a build reads back each round. A
+// device-to-host copy into pageable memory is staged by the driver and
+// keeps the calling thread inside the runtime until the stream has drained;
+// the drafter launches its decode step from another thread while a
+// background rebuild waits here, so the counts land in page-locked memory
+// instead: a pool of slots allocated once per process, one slot per build
+// in flight (a build that finds the pool empty uses its stack).
+constexpr int kCountSlots = 64;
+static std::mutex g_count_mu;
+static int64_t* g_count_pool = nullptr;
+static bool g_count_pool_failed = false;
+static uint64_t g_count_used = 0;  // bit i: slot i taken
+
+class CountSlot {
+ public:
+  CountSlot() {
+    std::lock_guard<std::mutex> lk(g_count_mu);
+    if (!g_count_pool && !g_count_pool_failed) {
+      void* p = nullptr;
+      if (cudaHostAlloc(&p, kCountSlots * 64, cudaHostAllocDefault) ==
+          cudaSuccess) {
+        g_count_pool = static_cast<int64_t*>(p);
+      } else {
+        cudaGetLastError();
+        g_count_pool_failed = true;
+      }
+    }
+    if (!g_count_pool) return;
+    for (int i = 0; i < kCountSlots; ++i) {
+      if (!(g_count_used >> i & 1)) {
+        g_count_used |= uint64_t(1) << i;
+        idx_ = i;
+        ptr_ = g_count_pool + i * 8;  // one 64-byte line per slot
+        return;
+      }
+    }
+  }
+  ~CountSlot() {
+    if (idx_ < 0) return;
+    std::lock_guard<std::mutex> lk(g_count_mu);
+    g_count_used &= ~(uint64_t(1) << idx_);
+  }
+  CountSlot(const CountSlot&) = delete;
+  CountSlot& operator=(const CountSlot&) = delete;
+  int64_t* get() { return ptr_ ? ptr_ : &fallback_; }
+
+ private:
+  int idx_ = -1;
+  int64_t* ptr_ = nullptr;
+  int64_t fallback_ = 0;
+};
+
+// Reads a device count into *out (host sync), through the build's slot.
+static int read_count(const int64_t* dev, int64_t* out, CountSlot& slot,
+                      cudaStream_t st) {
+  int64_t* land = slot.get();
+  cudaError_t e = cudaMemcpyAsync(land, dev, sizeof(int64_t),
                                   cudaMemcpyDeviceToHost, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return SG_ERR_CUDA;
   }
+  *out = *land;
   return SG_OK;
 }
 
@@ -694,7 +749,7 @@ static int read_count(const int64_t* dev, int64_t* out, cudaStream_t st) {
 // (group, second key) into (K[1], V[1]): small groups on chip, large ones
 // through the global radix sort.
 static int segmented_sort(SaWorkspace& w, int64_t m, int sb, int bits,
-                          cudaStream_t st) {
+                          CountSlot& slot, cudaStream_t st) {
   const int nseg = static_cast<int>((m + kSegTile - 1) / kSegTile);
   const size_t seg_smem = static_cast<size_t>(kSegWin) * 16;
   seg_local_kernel<<<nseg, kSegThreads, seg_smem, st>>>(
@@ -705,7 +760,7 @@ static int segmented_sort(SaWorkspace& w, int64_t m, int sb, int bits,
   round_scan_blocks_kernel<<<1, 1024, 0, st>>>(w.blk_max, w.blk_sum, nblk,
                                                w.m_dev);
   int64_t ml = 0;
-  const int rc = read_count(w.m_dev, &ml, st);
+  const int rc = read_count(w.m_dev, &ml, slot, st);
   if (rc != SG_OK) return rc;
   if (ml == 0) return SG_OK;
   flag_compact_kernel<<<nblk, kScanThreads, 0, st>>>(
@@ -721,7 +776,8 @@ static int segmented_sort(SaWorkspace& w, int64_t m, int sb, int bits,
 // One apply pass; returns the next active count (host sync).
 static int apply_round(SaWorkspace& w, int kcur, const uint32_t* act,
                        uint32_t* act_next, int64_t m, int32_t* sa,
-                       cudaStream_t st, int64_t* next_m, int* err) {
+                       CountSlot& slot, cudaStream_t st, int64_t* next_m,
+                       int* err) {
   const int nblk = static_cast<int>((m + kScanBlock - 1) / kScanBlock);
   round_reduce_kernel<<<nblk, kScanThreads, 0, st>>>(w.K[kcur], act, m,
                                                     w.blk_max, w.blk_sum);
@@ -730,12 +786,9 @@ static int apply_round(SaWorkspace& w, int kcur, const uint32_t* act,
   round_apply_kernel<<<nblk, kScanThreads, 0, st>>>(
       w.K[kcur], w.V[kcur], act, m, w.blk_max, w.blk_sum, sa, w.rank,
       act_next);
-  cudaError_t e = cudaMemcpyAsync(next_m, w.m_dev, sizeof(int64_t),
-                                  cudaMemcpyDeviceToHost, st);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-  if (e != cudaSuccess) {
-    set_cuda_error(e);
-    *err = SG_ERR_CUDA;
+  const int rc = read_count(w.m_dev, next_m, slot, st);
+  if (rc != SG_OK) {
+    *err = rc;
     return 0;
   }
   return 1;
@@ -771,6 +824,7 @@ extern "C" int sg_build_suffix_array(const int32_t* tokens, int64_t n,
   if (!workspace || ws_bytes < carve(nullptr, n).bytes)
     return SG_ERR_WORKSPACE;
   SaWorkspace w = carve(workspace, n);
+  CountSlot slot;
 
   // initial pass: sort by the first token
   init_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(
@@ -779,7 +833,8 @@ extern "C" int sg_build_suffix_array(const int32_t* tokens, int64_t n,
   int err = SG_OK;
   int64_t m = 0;
   int acur = 0;
-  if (!apply_round(w, kcur, nullptr, w.act[acur], n, sa_out, st, &m, &err))
+  if (!apply_round(w, kcur, nullptr, w.act[acur], n, sa_out, slot, st, &m,
+                   &err))
     return err;
   const int sb = bitlen(static_cast<uint64_t>(n));        // rank[i+h]+1 <= n
   const int pb = bitlen(static_cast<uint64_t>(n - 1));    // group start < n
@@ -788,12 +843,12 @@ extern "C" int sg_build_suffix_array(const int32_t* tokens, int64_t n,
     if (h >= n) return SG_ERR_CUDA;  // cannot happen for a correct build
     make_keys_kernel<<<static_cast<unsigned>((m + 255) / 256), 256, 0, st>>>(
         w.act[acur], sa_out, w.rank, n, m, h, sb, w.K[0], w.V[0]);
-    const int rc = segmented_sort(w, m, sb, pb + sb, st);
+    const int rc = segmented_sort(w, m, sb, pb + sb, slot, st);
     if (rc != SG_OK) return rc;
     kcur = 1;
     int64_t m_next = 0;
-    if (!apply_round(w, kcur, w.act[acur], w.act[1 - acur], m, sa_out, st,
-                     &m_next, &err))
+    if (!apply_round(w, kcur, w.act[acur], w.act[1 - acur], m, sa_out, slot,
+                     st, &m_next, &err))
       return err;
     acur = 1 - acur;
     m = m_next;

@@ -17,7 +17,9 @@ first ``poll_rebuild`` after it has finished, as in the reference.
 
 from __future__ import annotations
 
+import queue
 import threading
+import weakref
 from collections import deque
 
 import torch
@@ -97,6 +99,16 @@ class _ThreadEvent:
         self._done.wait()
 
 
+def _serve_builds(jobs: queue.SimpleQueue) -> None:
+    """Body of an index's build thread: runs queued builds until None."""
+    while True:
+        job = jobs.get()
+        if job is None:
+            return
+        job()
+        del job  # the job holds the index; do not keep it while idle
+
+
 class GlobalIndex:
     """GPU-resident global suffix index with periodic rebuilds."""
 
@@ -133,7 +145,10 @@ class GlobalIndex:
         self.delta_doc_lens: list[int] = []
         self._rebuild_event = None
         self._pending = None
+        # one long-lived build thread per index (started on first use): a
+        # queue hand-off per rebuild instead of a thread start
         self._worker: threading.Thread | None = None
+        self._jobs: queue.SimpleQueue | None = None
         self.rebuilds = 0
         self.last_rounds = 0
         self._sa_ws: torch.Tensor | None = None
@@ -292,8 +307,13 @@ class GlobalIndex:
                     ev.error = e
                 ev.set()
 
-            self._worker = threading.Thread(target=work, daemon=True)
-            self._worker.start()
+            if self._worker is None:
+                self._jobs = queue.SimpleQueue()
+                self._worker = threading.Thread(
+                    target=_serve_builds, args=(self._jobs,), daemon=True)
+                self._worker.start()
+                weakref.finalize(self, self._jobs.put, None)
+            self._jobs.put(work)
         else:
             self._build_staging_sa(dst, m, None)
             self._finish_swap(n_new, new_doc_lens)
@@ -320,7 +340,6 @@ class GlobalIndex:
         self.active_doc_lens = new_doc_lens
         self._rebuild_event = None
         self._pending = None
-        self._worker = None
         self.rebuilds += 1
 
     def poll_rebuild(self) -> None:
