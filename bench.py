@@ -556,6 +556,7 @@ def run_global(args, dev) -> dict:
     torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t0
     prefill_rebuilds = gi.rebuilds
+    prefill_builds = len(gi.build_log)
     tok = torch.from_numpy(data["token_ids"]).to(dev)
     n = torch.from_numpy(data["num_tokens"]).to(dev)
     q_host = data["num_tokens"].astype(int).tolist()
@@ -580,6 +581,26 @@ def run_global(args, dev) -> dict:
     ms = e0.elapsed_time(e1) / args.global_steps
     rebuilds = gi.rebuilds - r0
     gi.wait_rebuild()
+    log = list(gi.build_log)
+
+    def build_stats(entries):
+        out = {}
+        for kind in ("append", "full"):
+            ts = [t for k, t, _ in entries if k == kind]
+            out[kind] = {"builds": len(ts),
+                         "mean_ms": 1e3 * sum(ts) / len(ts) if ts else None}
+        return out
+    # one full build of the final snapshot, for comparison
+    from suffixgpu_b200 import ops
+    m_fin = min(gi.active_len + 1, gi.capacity)
+    scratch = torch.empty(m_fin, dtype=torch.int32, device=dev)
+    ops.build_suffix_array_into(gi.corpus[:m_fin], scratch)
+    torch.cuda.synchronize()
+    tf = time.perf_counter()
+    ops.build_suffix_array_into(gi.corpus[:m_fin], scratch)
+    torch.cuda.synchronize()
+    full_same_ms = (time.perf_counter() - tf) * 1e3
+    del scratch
     # the propose step alone, replayed from a CUDA graph (no harvest)
     n_g = torch.from_numpy(data["num_tokens"]).to(dev)
     tok_g = tok.clone()
@@ -612,6 +633,14 @@ def run_global(args, dev) -> dict:
             "rebuilds_in_timed_steps": rebuilds,
             "active_corpus_tokens": gi.active_len,
             "prefill_s": prefill_s, "prefill_rebuilds": prefill_rebuilds,
+            "suffix_array_builds": {
+                "prefill": build_stats(log[:prefill_builds]),
+                "loop": build_stats(log[prefill_builds:]),
+                "full_build_of_final_snapshot_ms": full_same_ms,
+                "note": "append = incremental merge into the previous "
+                        "suffix array (sg_suffix_array_append), full = "
+                        "from-scratch build; host wall time of each build "
+                        "on its stream (background thread in the loop)"},
             "graph_propose_us": graph_us,
             "graph_propose_rows_per_s": b / (graph_us * 1e-6),
             "workload": "config3: 4096 x 1024 template corpus (64 templates "

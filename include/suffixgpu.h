@@ -183,6 +183,30 @@ int sg_build_suffix_array_noalloc(const int32_t* tokens, int64_t n,
                                   int32_t* sa_out, int32_t* rounds_out,
                                   sg_stream_t stream);
 
+/* Workspace bytes sg_suffix_array_append needs for n tokens (~48 n). */
+size_t sg_suffix_array_append_workspace_size(int64_t n);
+
+/* Incremental rebuild (the staging build of GlobalIndex._launch_rebuild,
+ * global_index.py:147-223, without re-sorting the kept corpus; the
+ * reference rebuilds from scratch). sa_out[0..n) = the suffix array of
+ * tokens[0..n), identical to sg_build_suffix_array's, given:
+ *   tokens[0..kept) == the previous snapshot's tokens[evicted..evicted+kept)
+ *   prev_sa[0..prev_n) = the suffix array of the previous snapshot (length
+ *     prev_n, evicted + kept <= prev_n),
+ *   prev_rounds = the rounds its build reported (its longest common prefix
+ *     of two suffixes is below 2^prev_rounds).
+ * The suffixes with more than 2^prev_rounds kept tokens left keep their
+ * previous order; the rest are sorted by the full builder and merged in.
+ * rounds_out (host, may be NULL) receives the new snapshot's bound, to be
+ * passed as prev_rounds to the next call. Synchronises `stream` like
+ * sg_build_suffix_array; prev_sa and sa_out must not overlap. */
+int sg_suffix_array_append(const int32_t* tokens, int64_t n,
+                           const int32_t* prev_sa, int64_t prev_n,
+                           int64_t evicted, int64_t kept,
+                           int32_t prev_rounds, int32_t* sa_out,
+                           void* workspace, size_t workspace_bytes,
+                           int32_t* rounds_out, sg_stream_t stream);
+
 /* ---- suffix-array search (suffix_gpu/sa_search.py) ---------------------- */
 
 /* search_interval (sa_search.py:66-107, triton_kernels.py:284-302): SA

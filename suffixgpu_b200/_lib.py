@@ -78,6 +78,9 @@ _SIGS: dict[str, list] = {
                               c_size_t, POINTER(c_int32), c_void_p],
     "sg_build_suffix_array_noalloc": [c_void_p, c_int64, c_void_p,
                                       POINTER(c_int32), c_void_p],
+    "sg_suffix_array_append": [c_void_p, c_int64, c_void_p, c_int64, c_int64,
+                               c_int64, c_int32, c_void_p, c_void_p, c_size_t,
+                               POINTER(c_int32), c_void_p],
     "sg_sa_search": [c_void_p, c_void_p, c_int64, c_void_p, c_int32, c_int32,
                      c_void_p, c_void_p, c_void_p, c_void_p],
     "sg_suffix_match_backoff": [c_void_p, c_void_p, c_int64, c_void_p,
@@ -135,6 +138,7 @@ def lib() -> ctypes.CDLL:
 # entry points with non-int return types: name -> (restype, argtypes)
 _SIGS_EXTRA: dict[str, tuple] = {
     "sg_suffix_array_workspace_size": (c_size_t, [c_int64]),
+    "sg_suffix_array_append_workspace_size": (c_size_t, [c_int64]),
 }
 
 

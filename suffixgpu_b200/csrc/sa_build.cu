@@ -745,6 +745,12 @@ static int read_count(const int64_t* dev, int64_t* out, CountSlot& slot,
   return SG_OK;
 }
 
+// One read through a slot of its own, for callers outside a build loop.
+int read_device_i64(const int64_t* dev, int64_t* out, cudaStream_t st) {
+  CountSlot slot;
+  return read_count(dev, out, slot, st);
+}
+
 // Orders the active list (K[0], V[0]; m elements, grouped) by
 // (group, second key) into (K[1], V[1]): small groups on chip, large ones
 // through the global radix sort.

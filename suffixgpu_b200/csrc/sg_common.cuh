@@ -22,6 +22,10 @@ inline int check_launch() {
   return SG_OK;
 }
 
+// Reads one device int64 into *out through page-locked memory and
+// synchronises `st` (the suffix-array builds' host round trip).
+int read_device_i64(const int64_t* dev, int64_t* out, cudaStream_t st);
+
 // Returns the device's max dynamic shared memory per block (opt-in).
 int max_dyn_smem();
 int num_sms();

@@ -19,6 +19,7 @@ from __future__ import annotations
 
 import queue
 import threading
+import time
 import weakref
 from collections import deque
 
@@ -30,6 +31,11 @@ from suffixgpu_b200._lib import call, check, lib, ptr, stream_of
 PAD_TOKEN = torch.iinfo(torch.int32).max
 SEP_TOKEN = -2
 _UNSUPPORTED = 4  # SG_ERR_UNSUPPORTED
+# Incremental rebuilds only while the active SA's common prefixes are below
+# 2^12 tokens: the merge re-sorts the last 2^rounds kept tokens and its
+# comparisons can run that deep (on a corpus of exactly repeated 256K-token
+# stretches the merge took 12 ms against 4.2 ms for a full build).
+_APPEND_MAX_ROUNDS = 12
 
 
 def plan_bulk_load(active_doc_lens, active_len: int, new_doc_lens,
@@ -152,6 +158,17 @@ class GlobalIndex:
         self.rebuilds = 0
         self.last_rounds = 0
         self._sa_ws: torch.Tensor | None = None
+        # Incremental rebuilds (sg_suffix_array_append): the staging SA is
+        # merged from the active one when at most half of the snapshot has
+        # to be sorted afresh. _sa_rounds bounds the active SA's longest
+        # common prefix (< 2^_sa_rounds; None when unknown, e.g. after
+        # load_state_dict of an old state); the empty index's SA is exact.
+        self.incremental_rebuild = True
+        self._sa_rounds: int | None = 0
+        self._staging_rounds: int | None = None
+        self.last_build = None  # "full" or "append"
+        # (kind, host seconds, snapshot tokens) of the latest builds
+        self.build_log: deque = deque(maxlen=1024)
         # Multi-GPU: maps "my rebuild has finished" to "every rank's has",
         # so that replicas of the index swap at the same call.
         self.rebuild_agree = None
@@ -285,12 +302,7 @@ class GlobalIndex:
 
         # Build over the real prefix plus one sentinel column.
         m = min(n_new + 1, self.capacity)
-        if self._sa_ws is None:
-            from suffixgpu_b200 import _lib
-            need = int(_lib.lib().sg_suffix_array_workspace_size(
-                self.capacity))
-            self._sa_ws = torch.empty(need, dtype=torch.uint8,
-                                      device=self.device)
+        plan = self._build_plan(m, keep_start, n_active_keep)
         if self.rebuild_stream is not None:
             self.rebuild_stream.wait_stream(
                 torch.cuda.current_stream(self.device))
@@ -302,7 +314,7 @@ class GlobalIndex:
                 try:
                     with torch.cuda.device(self.device):
                         self._build_staging_sa(
-                            dst, m, self.rebuild_stream.cuda_stream)
+                            dst, m, self.rebuild_stream.cuda_stream, plan)
                 except BaseException as e:  # surfaced at poll time
                     ev.error = e
                 ev.set()
@@ -315,14 +327,46 @@ class GlobalIndex:
                 weakref.finalize(self, self._jobs.put, None)
             self._jobs.put(work)
         else:
-            self._build_staging_sa(dst, m, None)
+            self._build_staging_sa(dst, m, None, plan)
             self._finish_swap(n_new, new_doc_lens)
 
+    def _build_plan(self, m: int, evicted: int, kept: int):
+        """How to build a staging snapshot of m tokens whose first `kept`
+        are the active corpus from `evicted` on: None for a full build, or
+        the arguments of an incremental one (decided and captured on the
+        calling thread)."""
+        if self._sa_ws is None:
+            from suffixgpu_b200 import _lib
+            need = int(_lib.lib().sg_suffix_array_append_workspace_size(
+                self.capacity))
+            self._sa_ws = torch.empty(need, dtype=torch.uint8,
+                                      device=self.device)
+        r = self._sa_rounds
+        if not self.incremental_rebuild or r is None or kept <= 0:
+            return None
+        if r > _APPEND_MAX_ROUNDS:
+            return None  # long repeats: merge comparisons would run deep
+        if 2 * (kept - (1 << r)) < m:
+            return None  # over half of the snapshot would be re-sorted
+        prev_n = min(self.active_len + 1, self.capacity)
+        return (prev_n, evicted, kept, r)
+
     def _build_staging_sa(self, dst: torch.Tensor, m: int,
-                          stream: int | None) -> None:
-        self.last_rounds = ops.build_suffix_array_into(
-            dst[:m], self.staging_sa[:m], workspace=self._sa_ws,
-            stream=stream)
+                          stream: int | None, plan=None) -> None:
+        t0 = time.perf_counter()
+        if plan is None:
+            self.last_rounds = ops.build_suffix_array_into(
+                dst[:m], self.staging_sa[:m], workspace=self._sa_ws,
+                stream=stream)
+            self.last_build = "full"
+        else:
+            prev_n, evicted, kept, r = plan
+            self.last_rounds = ops.append_suffix_array_into(
+                dst[:m], self.staging_sa[:m], self.sa, prev_n, evicted,
+                kept, r, workspace=self._sa_ws, stream=stream)
+            self.last_build = "append"
+        self._staging_rounds = self.last_rounds
+        self.build_log.append((self.last_build, time.perf_counter() - t0, m))
         if m < self.capacity:
             # all-sentinel suffixes compare greater than any real pattern
             if stream is None:
@@ -338,6 +382,7 @@ class GlobalIndex:
         self.sa.copy_(self.staging_sa)
         self.active_len = n_new
         self.active_doc_lens = new_doc_lens
+        self._sa_rounds = self._staging_rounds
         self._rebuild_event = None
         self._pending = None
         self.rebuilds += 1
@@ -409,12 +454,9 @@ class GlobalIndex:
             acc += ln
         new_doc_lens.extend(reversed(kept_old))
         new_doc_lens.extend(new_lens[first:first + count])
-        if self._sa_ws is None:
-            from suffixgpu_b200 import _lib
-            need = int(_lib.lib().sg_suffix_array_workspace_size(cap))
-            self._sa_ws = torch.empty(need, dtype=torch.uint8,
-                                      device=self.device)
-        self._build_staging_sa(dst, min(n_new + 1, cap), None)
+        m = min(n_new + 1, cap)
+        plan = self._build_plan(m, self.active_len - keep, keep)
+        self._build_staging_sa(dst, m, None, plan)
         self._finish_swap(n_new, new_doc_lens)
 
     def state_dict(self) -> dict:
@@ -431,6 +473,7 @@ class GlobalIndex:
             "delta": self.delta[:self.delta_len].cpu(),
             "active_doc_lens": list(self.active_doc_lens),
             "delta_doc_lens": list(self.delta_doc_lens),
+            "sa_rounds": self._sa_rounds,
         }
 
     def load_state_dict(self, state: dict) -> None:
@@ -455,6 +498,8 @@ class GlobalIndex:
         self.active_len = n
         self.active_doc_lens = deque(int(x) for x in state["active_doc_lens"])
         self.delta_doc_lens = [int(x) for x in state["delta_doc_lens"]]
+        r = state.get("sa_rounds")
+        self._sa_rounds = None if r is None else int(r)
 
     def wait_rebuild(self) -> None:
         """Block until an in-flight background rebuild has finished and

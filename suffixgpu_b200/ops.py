@@ -159,6 +159,38 @@ def build_suffix_array_into(tokens: torch.Tensor, out: torch.Tensor,
     return int(rounds.value)
 
 
+def append_suffix_array_into(tokens: torch.Tensor, out: torch.Tensor,
+                             prev_sa: torch.Tensor, prev_n: int,
+                             evicted: int, kept: int, prev_rounds: int,
+                             workspace: torch.Tensor | None = None,
+                             stream: int | None = None) -> int:
+    """Suffix array of the 1-D int32 tokens into `out` from the suffix
+    array of the previous snapshot (sg_suffix_array_append): tokens[:kept]
+    must equal the previous snapshot's tokens[evicted:evicted + kept],
+    prev_sa[:prev_n] be its suffix array and prev_rounds the rounds its
+    build reported. Returns the new snapshot's rounds bound. Synchronises
+    the stream it runs on."""
+    dev = require_cuda(tokens, out, prev_sa)
+    tokens = as_i32(tokens.reshape(-1))
+    n = tokens.numel()
+    if out.dtype != torch.int32 or out.numel() < n or not out.is_contiguous():
+        raise ValueError("out must be a contiguous int32 tensor of length n")
+    if (prev_sa.dtype != torch.int32 or not prev_sa.is_contiguous()
+            or prev_sa.numel() < prev_n):
+        raise ValueError("prev_sa must be a contiguous int32 tensor holding "
+                         "prev_n entries")
+    L = _lib.lib()
+    need = int(L.sg_suffix_array_append_workspace_size(n))
+    if workspace is None or workspace.numel() < need:
+        workspace = _workspace(dev, need, "sa_append")
+    rounds = _lib.c_int32(0)
+    call("sg_suffix_array_append", ptr(tokens), n, ptr(prev_sa), prev_n,
+         evicted, kept, prev_rounds, ptr(out), ptr(workspace),
+         workspace.numel(), _lib.ctypes.byref(rounds),
+         stream if stream is not None else stream_of(dev))
+    return int(rounds.value)
+
+
 def build_suffix_array(tokens: torch.Tensor) -> torch.Tensor:
     """build_suffix_array (suffix_array.py:15-63): int64 start positions of
     the suffixes in lexicographic order."""

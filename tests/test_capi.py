@@ -75,6 +75,18 @@ def test_invalid_arguments_rejected_without_gpu(libpath):
     assert st == 0  # empty batch: nothing to do
     assert L.sg_expand_chain(None, 1, 0, 4, None, None, 0.0, 0.0, None, None,
                              None, None, None) == 1
+    # incremental SA rebuild: kept part outside the previous snapshot,
+    # negative sizes, and an empty snapshot (nothing to do)
+    r = ctypes.c_int32(-1)
+    assert L.sg_suffix_array_append(None, 10, None, 10, 5, 6, 0, None, None,
+                                    0, ctypes.byref(r), None) == 1
+    assert L.sg_suffix_array_append(None, -1, None, 0, 0, 0, 0, None, None,
+                                    0, None, None) == 1
+    assert L.sg_suffix_array_append(None, 0, None, 0, 0, 0, 0, None, None,
+                                    0, ctypes.byref(r), None) == 0
+    assert r.value == 0
+    assert L.sg_suffix_array_append_workspace_size(1 << 20) >= \
+        L.sg_suffix_array_workspace_size(1 << 20)
 
 
 def test_torch_operator_registers():
