@@ -57,11 +57,15 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true",
                     help="skip the CPU baseline leg (profiling runs)")
     ap.add_argument("--mode", default="draft",
-                    choices=["draft", "sa", "global", "sharded"],
+                    choices=["draft", "sa", "global", "sharded", "vllm"],
                     help="draft: config 2 (+ SA build, SA query and "
                          "global-path lines); sa: SA build + queries only "
                          "(config 4); global: config 3 only; sharded: "
-                         "config 5 only (1..8 GPUs under torchrun)")
+                         "config 5 only (1..8 GPUs under torchrun); vllm: "
+                         "config 2 through the vLLM adapter's call "
+                         "sequence (1 GPU)")
+    ap.add_argument("--vllm-steps", type=int, default=2000,
+                    help="timed steps of --mode vllm")
     ap.add_argument("--sa-log2n", type=int, default=24,
                     help="SA build size (config 4: 2^24 tokens)")
     ap.add_argument("--sa-reps", type=int, default=5)
@@ -649,6 +653,105 @@ def run_global(args, dev) -> dict:
                         "2^16, threshold 32768, 4 harvests + poll per step"}
 
 
+def run_vllm(args, dev) -> dict:
+    """Config 2 through vLLM's ngram_gpu call sequence on the adapter
+    (suffixgpu_b200.vllm_adapter.SuffixGPUProposer): per step vLLM's own
+    update_token_ids_ngram (valid counts, next ids; torch ops) and the
+    adapter's propose, eager, as the V1 model runner issues them, over the
+    32 rotating replicas of the main bench. Beside it the same steps as one
+    direct propose_with_update call each. Both loops are host-bound; the
+    difference is the adapter's and vLLM's per-step overhead."""
+    import torch
+    from types import SimpleNamespace
+    from suffixgpu_b200 import SuffixGPUDrafter
+    from suffixgpu_b200 import workloads as wl
+    from suffixgpu_b200.vllm_adapter import SuffixGPUProposer
+    data = workload(0)
+    cfg = wl.CONFIG2_DRAFTER
+    spec = SimpleNamespace(
+        num_speculative_tokens=cfg["k"],
+        prompt_lookup_max=cfg["max_pattern_len"],
+        prompt_lookup_min=cfg.get("min_match_len", 1),
+        suffix_decoding_max_spec_factor=cfg.get("max_spec_factor"),
+        suffix_decoding_min_token_prob=cfg.get("min_token_prob", 0.0),
+        suffix_decoding_max_cached_requests=0)
+    vcfg = SimpleNamespace(speculative_config=spec,
+                           model_config=SimpleNamespace(max_model_len=S),
+                           scheduler_config=SimpleNamespace(max_num_seqs=B))
+    prop = SuffixGPUProposer(vcfg, dev,
+                             max_occurrences=cfg["max_occurrences"],
+                             num_backoff=cfg["num_backoff"])
+    direct = SuffixGPUDrafter(device=dev, **cfg)
+    shift = 7
+    tok0 = torch.from_numpy(data["token_ids"]).to(dev)
+    q0 = torch.from_numpy(data["num_tokens"]).to(dev)
+    samp0 = torch.from_numpy(data["sampled"]).to(dev)
+    reps = []
+    for r in range(NREP):
+        reps.append({"tok": torch.roll(tok0, shifts=shift * r,
+                                       dims=0).contiguous(),
+                     "cnt0": torch.roll(q0, shifts=shift * r,
+                                        dims=0).contiguous(),
+                     "samp": torch.roll(samp0, shifts=shift * r,
+                                        dims=1).contiguous()})
+    batch = SimpleNamespace(num_reqs=B, vocab_size=1 << 30)
+    discard = torch.zeros(B, dtype=torch.bool, device=dev)
+    n = args.vllm_steps
+
+    from vllm.v1.spec_decode.ngram_proposer_gpu import NgramProposerGPU
+    stock_update = NgramProposerGPU.update_token_ids_ngram
+
+    def loop(via_vllm, steps: int) -> float:
+        cur = [rp["cnt0"].clone() for rp in reps]
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        e0.record()
+        for i in range(steps):
+            r, j = i % NREP, (i // NREP) % DECODE_STEPS
+            rp = reps[r]
+            if j == 0:
+                cur[r] = rp["cnt0"].clone()
+            # vLLM keeps every count below max_model_len (its
+            # update_token_ids_ngram gathers token count - 1 from the row;
+            # a count past the row is out of range there), so both loops
+            # hold the config's overflowing rows at S - 1
+            if via_vllm:
+                update = (prop.update_token_ids_ngram if via_vllm != "stock"
+                          else (lambda *a: stock_update(prop, *a)))
+                _, counts, valid = update(rp["samp"][j], batch, rp["tok"],
+                                          cur[r], discard)
+                prop.propose(cur[r], rp["tok"], valid, counts)
+                cur[r] = torch.clamp(cur[r] + counts, max=S - 1)
+            else:
+                _, _, nxt = direct.propose_with_update(
+                    cur[r], rp["tok"], rp["samp"][j])
+                cur[r] = torch.clamp(nxt, max=S - 1)
+        e1.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        return e0.elapsed_time(e1) * 1e-3, wall
+
+    for mode in (True, "stock", False):
+        loop(mode, 3 * NREP)
+    dev_v, wall_v = loop(True, n)
+    dev_s, _ = loop("stock", n)
+    dev_d, wall_d = loop(False, n)
+    return {"metric": "propose rows/s through the vLLM ngram_gpu call "
+                      "sequence (config 2)",
+            "value": B * n / dev_v, "unit": "rows/s", "steps": n,
+            "us_per_step": dev_v * 1e6 / n,
+            "host_us_per_step": wall_v * 1e6 / n,
+            "direct_propose_with_update": {
+                "value": B * n / dev_d, "us_per_step": dev_d * 1e6 / n},
+            "with_vllm_stock_update_token_ids_ngram": {
+                "value": B * n / dev_s, "us_per_step": dev_s * 1e6 / n},
+            "workload": "config2 rows (B=256, S=8192, k=16, P=32, R=128), "
+                        "32 rotating replicas, eager, update_token_ids_ngram "
+                        "+ SuffixGPUProposer.propose per step"}
+
+
 def run_e2e(args, drafter, reps, data, dev, world):
     """Same metric through the public API: per step an H2D copy of the
     step's sampled ids from pinned host memory, the eager
@@ -791,6 +894,11 @@ def main():
     args = parse()
     if args.impl == "reference":
         res = run_reference(args)
+    elif args.mode == "vllm":
+        import torch
+        dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        torch.cuda.set_device(dev)
+        res = run_vllm(args, dev)
     elif args.mode in ("sa", "global"):
         import torch
         dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))

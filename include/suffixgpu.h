@@ -150,6 +150,26 @@ int sg_expand_chain(const int32_t* cont, int32_t rows, int32_t max_occ,
                     int64_t* num_valid, int64_t* num_emit, float* score,
                     sg_stream_t stream);
 
+/* ---- vLLM glue ----------------------------------------------------------- */
+
+/* The per-step preparation of vLLM's GPU n-gram proposer
+ * (vllm/v1/spec_decode/ngram_proposer_gpu.py, update_token_ids_ngram) in
+ * one launch; no reference counterpart (the reference ships no vLLM
+ * adapter). For each request row b < batch:
+ *   valid_sampled[b, :] = sampled[b, :cols], or -1s when discard[b] != 0
+ *   valid_count[b] = #(valid_sampled[b, j] != -1 and < vocab_size)
+ *   next_ids[b] = valid_sampled[b, valid_count[b] - 1] if valid_count[b] > 0
+ *                 else token_ids[b, clamp(num_tokens[b] - 1, 0, seq_len - 1)]
+ * sampled is [batch, sampled_stride] (cols used), valid_sampled is
+ * [batch, cols] contiguous, discard may be NULL (no discards). */
+int sg_vllm_prepare(const int32_t* sampled, int64_t sampled_stride,
+                    int32_t batch, int32_t cols, const uint8_t* discard,
+                    const int32_t* token_ids, int64_t row_stride,
+                    int32_t seq_len, const int32_t* num_tokens,
+                    int64_t vocab_size, int32_t* next_ids,
+                    int32_t* valid_count, int32_t* valid_sampled,
+                    sg_stream_t stream);
+
 /* ---- suffix array (suffix_gpu/suffix_array.py) -------------------------- */
 
 /* Workspace bytes sg_build_suffix_array needs for n tokens (~36 n). */

@@ -7,6 +7,8 @@
 // current torch stream. The drafter's settings arrive as a small host
 // tensor holding an sg_draft_params struct; the batch shape comes from
 // token_ids. Errors raise (TORCH_CHECK) with the library's status string.
+// suffixgpu_b200::vllm_prepare wraps sg_vllm_prepare, the per-step input
+// preparation of vLLM's GPU n-gram proposer, for the vLLM adapter.
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
@@ -100,6 +102,52 @@ std::vector<at::Tensor> local_draft(const at::Tensor& num_tokens,
   return res;
 }
 
+// vLLM's update_token_ids_ngram (ngram_proposer_gpu.py) in one launch:
+// returns [next_token_ids [B] int32, valid_sampled_tokens_count [B] int32,
+// valid_sampled_token_ids [B, T] int32], B = sampled.size(0).
+std::vector<at::Tensor> vllm_prepare(const at::Tensor& sampled,
+                                     const c10::optional<at::Tensor>& discard,
+                                     const at::Tensor& token_ids,
+                                     const at::Tensor& num_tokens,
+                                     int64_t vocab_size) {
+  TORCH_CHECK(sampled.is_cuda() && token_ids.is_cuda() && num_tokens.is_cuda(),
+              "suffixgpu_b200 ops need CUDA tensors");
+  TORCH_CHECK(sampled.scalar_type() == at::kInt && sampled.dim() == 2,
+              "sampled must be an int32 [B, T] tensor");
+  TORCH_CHECK(token_ids.scalar_type() == at::kInt && token_ids.dim() == 2 &&
+                  token_ids.stride(1) == 1,
+              "token_ids must be an int32 [B, S] tensor with unit column stride");
+  const c10::cuda::CUDAGuard guard(token_ids.device());
+  at::Tensor samp = sampled.stride(1) == 1 ? sampled : sampled.contiguous();
+  const int64_t b = samp.size(0), t = samp.size(1);
+  TORCH_CHECK(token_ids.size(0) >= b && num_tokens.numel() >= b,
+              "token_ids / num_tokens have fewer rows than sampled");
+  at::Tensor n = num_tokens;
+  if (n.scalar_type() != at::kInt || !n.is_contiguous())
+    n = n.to(at::kInt).contiguous();
+  at::Tensor disc;
+  const uint8_t* dptr = nullptr;
+  if (discard.has_value()) {
+    TORCH_CHECK(discard->numel() >= b, "discard has fewer rows than sampled");
+    disc = discard->to(at::kBool).contiguous();
+    dptr = reinterpret_cast<const uint8_t*>(disc.data_ptr<bool>());
+  }
+  at::Tensor buf = at::empty({b * (2 + t)}, token_ids.options());
+  int32_t* base = buf.data_ptr<int32_t>();
+  const int st = sg_vllm_prepare(
+      samp.data_ptr<int32_t>(), t > 0 ? samp.stride(0) : 0,
+      static_cast<int32_t>(b), static_cast<int32_t>(t), dptr,
+      token_ids.data_ptr<int32_t>(), token_ids.stride(0),
+      static_cast<int32_t>(token_ids.size(1)), n.data_ptr<int32_t>(),
+      vocab_size, base, base + b, base + 2 * b,
+      reinterpret_cast<sg_stream_t>(
+          c10::cuda::getCurrentCUDAStream(token_ids.device().index()).stream()));
+  TORCH_CHECK(st == SG_OK, "sg_vllm_prepare failed: ", sg_status_string(st),
+              " (status ", st, ", cuda error ", sg_last_cuda_error(), ")");
+  return {buf.narrow(0, 0, b), buf.narrow(0, b, b),
+          buf.narrow(0, 2 * b, b * t).view({b, t})};
+}
+
 }  // namespace
 
 TORCH_LIBRARY(suffixgpu_b200, m) {
@@ -107,8 +155,12 @@ TORCH_LIBRARY(suffixgpu_b200, m) {
       "local_draft(Tensor num_tokens, Tensor token_ids, Tensor? sampled, "
       "Tensor? valid_count, Tensor? mask, Tensor params, int limit, "
       "bool extras) -> Tensor[]");
+  m.def(
+      "vllm_prepare(Tensor sampled, Tensor? discard, Tensor token_ids, "
+      "Tensor num_tokens, int vocab_size) -> Tensor[]");
 }
 
 TORCH_LIBRARY_IMPL(suffixgpu_b200, CUDA, m) {
   m.impl("local_draft", &local_draft);
+  m.impl("vllm_prepare", &vllm_prepare);
 }

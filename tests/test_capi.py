@@ -97,3 +97,5 @@ def test_torch_operator_registers():
     schema = str(op.default._schema)
     assert schema.startswith("suffixgpu_b200::local_draft(Tensor num_tokens")
     assert "Tensor params" in schema and "-> Tensor[]" in schema
+    schema = str(_lib.torch_ops().vllm_prepare.default._schema)
+    assert schema.startswith("suffixgpu_b200::vllm_prepare(Tensor sampled")
