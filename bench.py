@@ -57,13 +57,15 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true",
                     help="skip the CPU baseline leg (profiling runs)")
     ap.add_argument("--mode", default="draft",
-                    choices=["draft", "sa", "global", "sharded", "vllm"],
+                    choices=["draft", "sa", "global", "sharded", "vllm",
+                             "rebuild"],
                     help="draft: config 2 (+ SA build, SA query and "
                          "global-path lines); sa: SA build + queries only "
                          "(config 4); global: config 3 only; sharded: "
                          "config 5 only (1..8 GPUs under torchrun); vllm: "
                          "config 2 through the vLLM adapter's call "
-                         "sequence (1 GPU)")
+                         "sequence (1 GPU); rebuild: config-3 snapshot, "
+                         "incremental vs full suffix-array build (1 GPU)")
     ap.add_argument("--vllm-steps", type=int, default=2000,
                     help="timed steps of --mode vllm")
     ap.add_argument("--sa-log2n", type=int, default=24,
@@ -340,6 +342,69 @@ def sa_alg_bytes(n: int, rounds: int) -> float:
     import math
     kb = 2 * math.ceil(math.log2(n + 1))
     return 8 * n + rounds * n * (12 + 24 * math.ceil(kb / 8))
+
+
+def run_rebuild(args, dev) -> dict:
+    """The config-3 rebuild: the active corpus is 4 M tokens of template
+    documents (each with its SEP) + PAD, the next snapshot evicts the
+    oldest 32 documents and appends 32 finished 4096-token rows. Times the
+    snapshot's suffix array built from scratch and merged from the
+    previous one (sg_suffix_array_append), CUDA events around each call
+    (both synchronise the stream once or twice per doubling round), and
+    checks that the two arrays are identical."""
+    import torch
+    from suffixgpu_b200 import ops
+    from suffixgpu_b200 import workloads as wl
+    data = wl.config3(seed=3, steps=1)
+    docs = data["corpus_docs"]
+    sep = np.array([-2], dtype=np.int32)
+    pad = np.array([2 ** 31 - 1], dtype=np.int32)
+    n_docs = docs.shape[0]
+    old = np.concatenate([np.concatenate([d, sep]) for d in docs]
+                         + [pad]).astype(np.int32)
+    evict = 32 * (docs.shape[1] + 1)
+    rows = data["token_ids"][:32]
+    new_part = np.concatenate([np.concatenate([r, sep]) for r in rows])
+    kept = len(old) - 1 - evict
+    snap = np.concatenate([old[evict:-1], new_part, pad]).astype(np.int32)
+    t_old = torch.from_numpy(old).to(dev)
+    t_new = torch.from_numpy(snap).to(dev)
+    sa_old = torch.empty(len(old), dtype=torch.int32, device=dev)
+    r_old = ops.build_suffix_array_into(t_old, sa_old)
+    full = torch.empty(len(snap), dtype=torch.int32, device=dev)
+    inc = torch.empty(len(snap), dtype=torch.int32, device=dev)
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(max(3, args.sa_reps)):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return float(statistics.median(ts))
+    ms_full = timed(lambda: ops.build_suffix_array_into(t_new, full))
+    ms_inc = timed(lambda: ops.append_suffix_array_into(
+        t_new, inc, sa_old, len(old), evict, kept, r_old))
+    r_new = ops.append_suffix_array_into(t_new, inc, sa_old, len(old),
+                                         evict, kept, r_old)
+    if not torch.equal(full, inc):
+        raise RuntimeError("incremental suffix array differs from the full "
+                           "build")
+    n = len(snap)
+    return {"metric": "config-3 rebuild, suffix array of the next snapshot",
+            "value": n / (ms_inc * 1e-3) / 1e6, "unit": "Mtok/s",
+            "n_tokens": n, "ms_incremental": ms_inc, "ms_full": ms_full,
+            "speedup": ms_full / ms_inc, "previous_rounds": r_old,
+            "new_rounds": r_new, "tail_tokens": n - (kept - (1 << r_old)),
+            "identical": True,
+            "workload": f"config3 corpus ({n_docs} x {docs.shape[1]} "
+                        "template documents + SEP + PAD), evict 32 "
+                        "documents, append 32 rows of 4096 tokens"}
 
 
 def run_sa(args, dev) -> dict:
@@ -894,6 +959,11 @@ def main():
     args = parse()
     if args.impl == "reference":
         res = run_reference(args)
+    elif args.mode == "rebuild":
+        import torch
+        dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        torch.cuda.set_device(dev)
+        res = run_rebuild(args, dev)
     elif args.mode == "vllm":
         import torch
         dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))

@@ -31,8 +31,6 @@
 // rounds) or a tail suffix and its kept neighbour (measured by the merge).
 #include <cuda_runtime.h>
 
-#include <climits>
-
 #include "sg_common.cuh"
 
 namespace sg {
@@ -134,44 +132,78 @@ __global__ void __launch_bounds__(kAppThreads)
   }
 }
 
-// Token at i of the snapshot widened so that the end of the string sorts
-// below every token.
-__device__ __forceinline__ int64_t snap_sym(const int32_t* __restrict__ s,
-                                            int64_t m, int64_t i) {
-  return i < m ? static_cast<int64_t>(s[i]) : LLONG_MIN;
+// One 32-token step of a comparison of suffix a (kept) with suffix t
+// (tail, a < t) at offsets [off, off + 32), cut at lim. Suffix t is the
+// shorter one: where it has ended (t + o >= m) suffix a still has a token
+// (a + o < m), so the first such offset is a difference that makes a > t
+// (the end of a string sorts first); there every load is skipped. Returns
+// 0 if no difference below lim, else -1 / 1 with *l at the difference.
+__device__ __forceinline__ int cmp_step32(const int32_t* __restrict__ s,
+                                          int64_t m, int64_t a, int64_t t,
+                                          int64_t off, int64_t lim,
+                                          int64_t* l) {
+  const int lane = lane_id();
+  const int64_t o = off + lane;
+  const bool t_end = t + o >= m;
+  int32_t va = 0, vt = 0;
+  if (!t_end && o < lim) {
+    va = s[a + o];
+    vt = s[t + o];
+  }
+  const unsigned d =
+      __ballot_sync(SG_FULL_MASK, o < lim && (t_end || va != vt));
+  if (!d) return 0;
+  const int b = __ffs(d) - 1;
+  const bool e = __shfl_sync(SG_FULL_MASK, t_end, b);
+  const int32_t xa = __shfl_sync(SG_FULL_MASK, va, b);
+  const int32_t xt = __shfl_sync(SG_FULL_MASK, vt, b);
+  *l = off + b;
+  return (e || xa > xt) ? 1 : -1;
 }
 
 // Warp-wide three-way comparison of suffix a (kept) with suffix t (tail,
 // t > a) from offset *l (a prefix both are known to share) up to offset
 // lim: -1 if a < t, 1 if a > t, 0 if they agree through lim - 1. *l leaves
-// as the longest common prefix (lim for 0). 128 tokens per step: four
-// coalesced loads per lane and side, issued together. With lim > m - t the
-// result is never 0 (suffix t ends first, against a token of a).
+// as the longest common prefix (lim for 0). Most comparisons of a binary
+// search end within a few tokens, so the first step reads 32 tokens per
+// side; longer ones continue 128 tokens per step (four independent 32-token
+// loads per side in flight). With lim > m - t the result is never 0.
 __device__ __forceinline__ int warp_cmp_upto(const int32_t* __restrict__ s,
                                              int64_t m, int64_t a, int64_t t,
                                              int64_t* l, int64_t lim) {
+  int64_t off = *l;
+  if (off < lim) {
+    const int c = cmp_step32(s, m, a, t, off, lim, l);
+    if (c) return c;
+    off += 32;
+  }
   const int lane = lane_id();
-  for (int64_t off = *l; off < lim; off += 128) {
+  for (; off < lim; off += 128) {
     const int64_t o0 = off + lane, o1 = o0 + 32, o2 = o0 + 64, o3 = o0 + 96;
-    const int64_t a0 = snap_sym(s, m, a + o0), t0 = snap_sym(s, m, t + o0);
-    const int64_t a1 = snap_sym(s, m, a + o1), t1 = snap_sym(s, m, t + o1);
-    const int64_t a2 = snap_sym(s, m, a + o2), t2 = snap_sym(s, m, t + o2);
-    const int64_t a3 = snap_sym(s, m, a + o3), t3 = snap_sym(s, m, t + o3);
-    const unsigned d0 = __ballot_sync(SG_FULL_MASK, o0 < lim && a0 != t0);
-    const unsigned d1 = __ballot_sync(SG_FULL_MASK, o1 < lim && a1 != t1);
-    const unsigned d2 = __ballot_sync(SG_FULL_MASK, o2 < lim && a2 != t2);
-    const unsigned d3 = __ballot_sync(SG_FULL_MASK, o3 < lim && a3 != t3);
+    const bool e0 = t + o0 >= m, e1 = t + o1 >= m, e2 = t + o2 >= m,
+               e3 = t + o3 >= m;
+    int32_t a0 = 0, t0 = 0, a1 = 0, t1 = 0, a2 = 0, t2 = 0, a3 = 0, t3 = 0;
+    if (!e0 && o0 < lim) { a0 = s[a + o0]; t0 = s[t + o0]; }
+    if (!e1 && o1 < lim) { a1 = s[a + o1]; t1 = s[t + o1]; }
+    if (!e2 && o2 < lim) { a2 = s[a + o2]; t2 = s[t + o2]; }
+    if (!e3 && o3 < lim) { a3 = s[a + o3]; t3 = s[t + o3]; }
+    const unsigned d0 = __ballot_sync(SG_FULL_MASK, o0 < lim && (e0 || a0 != t0));
+    const unsigned d1 = __ballot_sync(SG_FULL_MASK, o1 < lim && (e1 || a1 != t1));
+    const unsigned d2 = __ballot_sync(SG_FULL_MASK, o2 < lim && (e2 || a2 != t2));
+    const unsigned d3 = __ballot_sync(SG_FULL_MASK, o3 < lim && (e3 || a3 != t3));
     if (d0 | d1 | d2 | d3) {
-      // first differing chunk j and lane b; its tokens from lane b
+      // first differing 32-token chunk j and lane b; values from lane b
       const int j = d0 ? 0 : d1 ? 1 : d2 ? 2 : 3;
       const unsigned d = j == 0 ? d0 : j == 1 ? d1 : j == 2 ? d2 : d3;
       const int b = __ffs(d) - 1;
-      const int64_t va = j == 0 ? a0 : j == 1 ? a1 : j == 2 ? a2 : a3;
-      const int64_t vt = j == 0 ? t0 : j == 1 ? t1 : j == 2 ? t2 : t3;
-      const int64_t xa = __shfl_sync(SG_FULL_MASK, va, b);
-      const int64_t xt = __shfl_sync(SG_FULL_MASK, vt, b);
+      const bool ej = j == 0 ? e0 : j == 1 ? e1 : j == 2 ? e2 : e3;
+      const int32_t aj = j == 0 ? a0 : j == 1 ? a1 : j == 2 ? a2 : a3;
+      const int32_t tj = j == 0 ? t0 : j == 1 ? t1 : j == 2 ? t2 : t3;
+      const bool e = __shfl_sync(SG_FULL_MASK, ej, b);
+      const int32_t xa = __shfl_sync(SG_FULL_MASK, aj, b);
+      const int32_t xt = __shfl_sync(SG_FULL_MASK, tj, b);
       *l = off + 32 * j + b;
-      return xa < xt ? -1 : 1;
+      return (e || xa > xt) ? 1 : -1;
     }
   }
   *l = lim;
