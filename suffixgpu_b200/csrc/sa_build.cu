@@ -39,10 +39,15 @@ constexpr int kSortThreads = 256;
 constexpr int kSortWarps = kSortThreads / 32;
 constexpr int kSortItems = 16;                    // keys per thread
 constexpr int kTile = kSortThreads * kSortItems;  // 4096 keys per tile
+// Small lists (fewer than two 4096-element tiles per SM: the rebuild's
+// tail sorts, short corpora) use 1024-element tiles in the sort and scan
+// passes, so that their blocks still cover the SMs.
+constexpr int kItemsSmall = 4;
 
 // ---------------------------------------------------------------------------
 // radix sort passes
 // ---------------------------------------------------------------------------
+template <int ITEMS>
 __global__ void __launch_bounds__(kSortThreads)
     rs_hist_kernel(const uint64_t* __restrict__ keys, int64_t m, int shift,
                    uint32_t* __restrict__ tile_hist, int ntiles,
@@ -51,9 +56,9 @@ __global__ void __launch_bounds__(kSortThreads)
   const int t = threadIdx.x, warp = warp_id();
   for (int i = t; i < kSortWarps * 256; i += kSortThreads) (&h[0][0])[i] = 0;
   __syncthreads();
-  const int64_t base = static_cast<int64_t>(blockIdx.x) * kTile;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kSortThreads * ITEMS;
 #pragma unroll
-  for (int r = 0; r < kSortItems; ++r) {
+  for (int r = 0; r < ITEMS; ++r) {
     const int64_t idx = base + r * kSortThreads + t;
     if (idx < m) atomicAdd(&h[warp][(keys[idx] >> shift) & 255], 1u);
   }
@@ -108,6 +113,7 @@ __global__ void zero_u32_kernel(uint32_t* p, int n) {
   if (i < n) p[i] = 0u;
 }
 
+template <int ITEMS>
 __global__ void __launch_bounds__(kSortThreads)
     rs_scatter_kernel(const uint64_t* __restrict__ kin,
                       const uint32_t* __restrict__ vin,
@@ -122,12 +128,12 @@ __global__ void __launch_bounds__(kSortThreads)
   s_off[t] = offs[static_cast<int64_t>(t) * ntiles + blockIdx.x];
   // warp w owns keys [base, base + 512) of the tile, 32 per round in order
   const int64_t base =
-      static_cast<int64_t>(blockIdx.x) * kTile + warp * (32 * kSortItems);
-  uint64_t key[kSortItems];
-  uint32_t val[kSortItems];
-  uint32_t loc[kSortItems];
+      static_cast<int64_t>(blockIdx.x) * kSortThreads * ITEMS + warp * (32 * ITEMS);
+  uint64_t key[ITEMS];
+  uint32_t val[ITEMS];
+  uint32_t loc[ITEMS];
 #pragma unroll
-  for (int r = 0; r < kSortItems; ++r) {
+  for (int r = 0; r < ITEMS; ++r) {
     const int64_t idx = base + r * 32 + lane;
     key[r] = idx < m ? kin[idx] : 0ull;
     val[r] = idx < m ? vin[idx] : 0u;
@@ -135,7 +141,7 @@ __global__ void __launch_bounds__(kSortThreads)
   __syncwarp();
   // stable rank of every key among this warp's keys with the same digit
 #pragma unroll
-  for (int r = 0; r < kSortItems; ++r) {
+  for (int r = 0; r < ITEMS; ++r) {
     const int64_t idx = base + r * 32 + lane;
     const bool valid = idx < m;
     const uint32_t d = static_cast<uint32_t>(key[r] >> shift) & 255u;
@@ -169,7 +175,7 @@ __global__ void __launch_bounds__(kSortThreads)
   }
   __syncthreads();
 #pragma unroll
-  for (int r = 0; r < kSortItems; ++r) {
+  for (int r = 0; r < ITEMS; ++r) {
     const int64_t idx = base + r * 32 + lane;
     if (idx < m) {
       const uint32_t d = static_cast<uint32_t>(key[r] >> shift) & 255u;
@@ -185,7 +191,6 @@ __global__ void __launch_bounds__(kSortThreads)
 // ---------------------------------------------------------------------------
 constexpr int kScanThreads = 256;
 constexpr int kScanItems = 16;
-constexpr int kScanBlock = kScanThreads * kScanItems;
 
 __global__ void init_keys_kernel(const int32_t* __restrict__ tok, int64_t n,
                                  uint64_t* __restrict__ keys,
@@ -227,15 +232,16 @@ __device__ __forceinline__ void round_flags(const uint64_t* K, int64_t m,
 
 // Per scan block: max of the new group starts and count of elements that
 // stay active.
+template <int ITEMS>
 __global__ void __launch_bounds__(kScanThreads)
     round_reduce_kernel(const uint64_t* __restrict__ K,
                         const uint32_t* __restrict__ act, int64_t m,
                         uint32_t* __restrict__ blk_max,
                         uint32_t* __restrict__ blk_sum) {
   __shared__ uint32_t sm[kSortWarps], ss[kSortWarps];
-  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanBlock;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanThreads * ITEMS;
   uint32_t mx = 0, sum = 0;
-  for (int r = 0; r < kScanItems; ++r) {
+  for (int r = 0; r < ITEMS; ++r) {
     const int64_t t = base + r * kScanThreads + threadIdx.x;
     if (t < m) {
       bool head, keep;
@@ -326,6 +332,7 @@ __global__ void __launch_bounds__(1024)
 // of its group's first element: act is increasing, so a max-scan over
 // head-marked act values finds it) and compacts the still-tied elements
 // into act_next, all in element order.
+template <int ITEMS>
 __global__ void __launch_bounds__(kScanThreads)
     round_apply_kernel(const uint64_t* __restrict__ K,
                        const uint32_t* __restrict__ V,
@@ -336,10 +343,10 @@ __global__ void __launch_bounds__(kScanThreads)
                        uint32_t* __restrict__ act_next) {
   __shared__ uint32_t wm[kSortWarps], ws[kSortWarps];
   const int lane = lane_id(), warp = warp_id();
-  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanBlock;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanThreads * ITEMS;
   uint32_t carry_m = blk_max[blockIdx.x];
   uint32_t carry_s = blk_sum[blockIdx.x];
-  for (int r = 0; r < kScanItems; ++r) {
+  for (int r = 0; r < ITEMS; ++r) {
     const int64_t t = base + r * kScanThreads + threadIdx.x;
     bool head = false, keep = false;
     uint32_t a = 0;
@@ -519,14 +526,15 @@ __global__ void __launch_bounds__(kSegThreads)
 
 // Per scan block: number of flagged elements (blk_max zeroed so that the
 // shared scan kernel can be reused).
+template <int ITEMS>
 __global__ void __launch_bounds__(kScanThreads)
     flag_count_kernel(const uint8_t* __restrict__ flag, int64_t m,
                       uint32_t* __restrict__ blk_max,
                       uint32_t* __restrict__ blk_sum) {
   __shared__ uint32_t ss[kSortWarps];
-  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanBlock;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanThreads * ITEMS;
   uint32_t sum = 0;
-  for (int r = 0; r < kScanItems; ++r) {
+  for (int r = 0; r < ITEMS; ++r) {
     const int64_t t = base + r * kScanThreads + threadIdx.x;
     if (t < m) sum += flag[t];
   }
@@ -542,6 +550,7 @@ __global__ void __launch_bounds__(kScanThreads)
 }
 
 // Flagged elements in order: LK[u] = K[t], LV[u] = V[t], LT[u] = t.
+template <int ITEMS>
 __global__ void __launch_bounds__(kScanThreads)
     flag_compact_kernel(const uint8_t* __restrict__ flag,
                         const uint64_t* __restrict__ K,
@@ -551,9 +560,9 @@ __global__ void __launch_bounds__(kScanThreads)
                         uint32_t* __restrict__ LT) {
   __shared__ uint32_t ws[kSortWarps];
   const int lane = lane_id(), warp = warp_id();
-  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanBlock;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanThreads * ITEMS;
   uint32_t carry = blk_sum[blockIdx.x];
-  for (int r = 0; r < kScanItems; ++r) {
+  for (int r = 0; r < ITEMS; ++r) {
     const int64_t t = base + r * kScanThreads + threadIdx.x;
     const bool f = t < m && flag[t];
     const unsigned bal = __ballot_sync(SG_FULL_MASK, f);
@@ -623,8 +632,10 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 static SaWorkspace carve(void* base, int64_t n) {
   SaWorkspace w{};
   const size_t un = static_cast<size_t>(n > 0 ? n : 1);
-  const size_t ntiles = (un + kTile - 1) / kTile;
-  const size_t nblk = (un + kScanBlock - 1) / kScanBlock;
+  // per-tile / per-block arrays sized for the small tiles
+  const size_t small = static_cast<size_t>(kSortThreads) * kItemsSmall;
+  const size_t ntiles = (un + small - 1) / small;
+  const size_t nblk = (un + small - 1) / small;
   char* p = static_cast<char*>(base);
   size_t o = 0;
   auto take = [&](size_t bytes) {
@@ -652,22 +663,44 @@ static SaWorkspace carve(void* base, int64_t n) {
   return w;
 }
 
+// Whether a list of m elements takes the small tiles.
+static bool small_tiles(int64_t m) {
+  return (m + kTile - 1) / kTile < 2 * static_cast<int64_t>(num_sms());
+}
+
+static int elems_per_block(int64_t m) {
+  return kSortThreads * (small_tiles(m) ? kItemsSmall : kSortItems);
+}
+
+template <int ITEMS>
+static void radix_pass(SaWorkspace& w, const uint64_t* kin,
+                       const uint32_t* vin, uint64_t* kout, uint32_t* vout,
+                       int64_t m, int shift, cudaStream_t st) {
+  const int ntiles = static_cast<int>(
+      (m + kSortThreads * ITEMS - 1) / (kSortThreads * ITEMS));
+  zero_u32_kernel<<<1, 256, 0, st>>>(w.totals, 256);
+  rs_hist_kernel<ITEMS><<<ntiles, kSortThreads, 0, st>>>(
+      kin, m, shift, w.tile_hist, ntiles, w.totals);
+  rs_scan_kernel<<<256, kSortThreads, 0, st>>>(w.tile_hist, ntiles,
+                                               w.totals);
+  rs_scatter_kernel<ITEMS><<<ntiles, kSortThreads, 0, st>>>(
+      kin, vin, kout, vout, m, shift, w.tile_hist, ntiles);
+}
+
 // Stable LSD sort of (kb[cur], vb[cur]) by the low `bits` bits, ping-
 // ponging between the two buffer pairs; returns the index holding the
 // result.
 static int radix_sort_pair(SaWorkspace& w, uint64_t* const kb[2],
                            uint32_t* const vb[2], int cur, int64_t m,
                            int bits, cudaStream_t st) {
-  const int ntiles = static_cast<int>((m + kTile - 1) / kTile);
+  const bool small = small_tiles(m);
   for (int shift = 0; shift < bits; shift += 8) {
-    zero_u32_kernel<<<1, 256, 0, st>>>(w.totals, 256);
-    rs_hist_kernel<<<ntiles, kSortThreads, 0, st>>>(
-        kb[cur], m, shift, w.tile_hist, ntiles, w.totals);
-    rs_scan_kernel<<<256, kSortThreads, 0, st>>>(w.tile_hist, ntiles,
-                                                 w.totals);
-    rs_scatter_kernel<<<ntiles, kSortThreads, 0, st>>>(
-        kb[cur], vb[cur], kb[1 - cur], vb[1 - cur], m, shift, w.tile_hist,
-        ntiles);
+    if (small)
+      radix_pass<kItemsSmall>(w, kb[cur], vb[cur], kb[1 - cur], vb[1 - cur],
+                              m, shift, st);
+    else
+      radix_pass<kSortItems>(w, kb[cur], vb[cur], kb[1 - cur], vb[1 - cur],
+                             m, shift, st);
     cur = 1 - cur;
   }
   return cur;
@@ -760,17 +793,27 @@ static int segmented_sort(SaWorkspace& w, int64_t m, int sb, int bits,
   const size_t seg_smem = static_cast<size_t>(kSegWin) * 16;
   seg_local_kernel<<<nseg, kSegThreads, seg_smem, st>>>(
       w.K[0], w.V[0], m, sb, w.K[1], w.V[1], w.flag);
-  const int nblk = static_cast<int>((m + kScanBlock - 1) / kScanBlock);
-  flag_count_kernel<<<nblk, kScanThreads, 0, st>>>(w.flag, m, w.blk_max,
-                                                   w.blk_sum);
+  const bool small = small_tiles(m);
+  const int nblk = static_cast<int>((m + elems_per_block(m) - 1) /
+                                    elems_per_block(m));
+  if (small)
+    flag_count_kernel<kItemsSmall><<<nblk, kScanThreads, 0, st>>>(
+        w.flag, m, w.blk_max, w.blk_sum);
+  else
+    flag_count_kernel<kScanItems><<<nblk, kScanThreads, 0, st>>>(
+        w.flag, m, w.blk_max, w.blk_sum);
   round_scan_blocks_kernel<<<1, 1024, 0, st>>>(w.blk_max, w.blk_sum, nblk,
                                                w.m_dev);
   int64_t ml = 0;
   const int rc = read_count(w.m_dev, &ml, slot, st);
   if (rc != SG_OK) return rc;
   if (ml == 0) return SG_OK;
-  flag_compact_kernel<<<nblk, kScanThreads, 0, st>>>(
-      w.flag, w.K[0], w.V[0], m, w.blk_sum, w.LK, w.LV, w.LT);
+  if (small)
+    flag_compact_kernel<kItemsSmall><<<nblk, kScanThreads, 0, st>>>(
+        w.flag, w.K[0], w.V[0], m, w.blk_sum, w.LK, w.LV, w.LT);
+  else
+    flag_compact_kernel<kScanItems><<<nblk, kScanThreads, 0, st>>>(
+        w.flag, w.K[0], w.V[0], m, w.blk_sum, w.LK, w.LV, w.LT);
   uint64_t* const kb[2] = {w.LK, w.K[0]};
   uint32_t* const vb[2] = {w.LV, w.V[0]};
   const int c = radix_sort_pair(w, kb, vb, 0, ml, bits, st);
@@ -784,14 +827,25 @@ static int apply_round(SaWorkspace& w, int kcur, const uint32_t* act,
                        uint32_t* act_next, int64_t m, int32_t* sa,
                        CountSlot& slot, cudaStream_t st, int64_t* next_m,
                        int* err) {
-  const int nblk = static_cast<int>((m + kScanBlock - 1) / kScanBlock);
-  round_reduce_kernel<<<nblk, kScanThreads, 0, st>>>(w.K[kcur], act, m,
-                                                    w.blk_max, w.blk_sum);
+  const bool small = small_tiles(m);
+  const int nblk = static_cast<int>((m + elems_per_block(m) - 1) /
+                                    elems_per_block(m));
+  if (small)
+    round_reduce_kernel<kItemsSmall><<<nblk, kScanThreads, 0, st>>>(
+        w.K[kcur], act, m, w.blk_max, w.blk_sum);
+  else
+    round_reduce_kernel<kScanItems><<<nblk, kScanThreads, 0, st>>>(
+        w.K[kcur], act, m, w.blk_max, w.blk_sum);
   round_scan_blocks_kernel<<<1, 1024, 0, st>>>(w.blk_max, w.blk_sum, nblk,
                                                w.m_dev);
-  round_apply_kernel<<<nblk, kScanThreads, 0, st>>>(
-      w.K[kcur], w.V[kcur], act, m, w.blk_max, w.blk_sum, sa, w.rank,
-      act_next);
+  if (small)
+    round_apply_kernel<kItemsSmall><<<nblk, kScanThreads, 0, st>>>(
+        w.K[kcur], w.V[kcur], act, m, w.blk_max, w.blk_sum, sa, w.rank,
+        act_next);
+  else
+    round_apply_kernel<kScanItems><<<nblk, kScanThreads, 0, st>>>(
+        w.K[kcur], w.V[kcur], act, m, w.blk_max, w.blk_sum, sa, w.rank,
+        act_next);
   const int rc = read_count(w.m_dev, next_m, slot, st);
   if (rc != SG_OK) {
     *err = rc;
