@@ -399,38 +399,47 @@ constexpr int kSegTile = 2048;   // active-list elements owned by a block
 constexpr int kSegHalo = 256;    // largest group ranked on chip
 constexpr int kSegItems = 11;    // window elements per thread
 constexpr int kSegWin = kSegTile + 2 * kSegHalo + 2;  // (+ one each side)
+constexpr int kSegWinPad = (kSegWin + 3) & ~3;       // 16-byte rows
+constexpr size_t kSegSmem = sizeof(uint64_t) * kSegWin + 8 * kSegWinPad;
 static_assert(kSegThreads * kSegItems >= kSegWin, "window does not fit");
 
 // Exclusive prefix max / suffix min over the threads of a block (one value
-// per thread; Hillis-Steele in shared memory).
+// per thread): warp scans with shuffles, then the warps' totals.
 __device__ __forceinline__ int block_excl_prefix_max(int v, int* buf) {
-  const int t = threadIdx.x;
-  buf[t] = v;
-  __syncthreads();
-  for (int o = 1; o < kSegThreads; o <<= 1) {
-    const int x = t >= o ? buf[t - o] : INT32_MIN;
-    __syncthreads();
-    if (t >= o) buf[t] = max(buf[t], x);
-    __syncthreads();
+  const int lane = lane_id(), warp = warp_id();
+  int inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int x = __shfl_up_sync(SG_FULL_MASK, inc, o);
+    if (lane >= o) inc = max(inc, x);
   }
-  const int r = t > 0 ? buf[t - 1] : INT32_MIN;
+  if (lane == 31) buf[warp] = inc;
   __syncthreads();
-  return r;
+  int carry = INT32_MIN;
+  for (int w = 0; w < warp; ++w) carry = max(carry, buf[w]);
+  int ex = __shfl_up_sync(SG_FULL_MASK, inc, 1);
+  if (lane == 0) ex = INT32_MIN;
+  __syncthreads();  // buf is reused by the next scan
+  return max(carry, ex);
 }
 
 __device__ __forceinline__ int block_excl_suffix_min(int v, int* buf) {
-  const int t = threadIdx.x;
-  buf[t] = v;
-  __syncthreads();
-  for (int o = 1; o < kSegThreads; o <<= 1) {
-    const int x = t + o < kSegThreads ? buf[t + o] : INT32_MAX;
-    __syncthreads();
-    if (t + o < kSegThreads) buf[t] = min(buf[t], x);
-    __syncthreads();
+  const int lane = lane_id(), warp = warp_id();
+  constexpr int kWarps = kSegThreads / 32;
+  int inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int x = __shfl_down_sync(SG_FULL_MASK, inc, o);
+    if (lane + o < 32) inc = min(inc, x);
   }
-  const int r = t + 1 < kSegThreads ? buf[t + 1] : INT32_MAX;
+  if (lane == 0) buf[warp] = inc;
   __syncthreads();
-  return r;
+  int carry = INT32_MAX;
+  for (int w = warp + 1; w < kWarps; ++w) carry = min(carry, buf[w]);
+  int ex = __shfl_down_sync(SG_FULL_MASK, inc, 1);
+  if (lane == 31) ex = INT32_MAX;
+  __syncthreads();
+  return min(carry, ex);
 }
 
 // Element w of the window is element x = t0 - kSegHalo - 1 + w of the
@@ -447,8 +456,8 @@ __global__ void __launch_bounds__(kSegThreads)
                      uint8_t* __restrict__ large) {
   extern __shared__ __align__(16) unsigned char seg_smem[];
   uint64_t* sk = reinterpret_cast<uint64_t*>(seg_smem);   // [kSegWin]
-  int* first = reinterpret_cast<int*>(sk + kSegWin);      // [kSegWin]
-  int* last = first + kSegWin;                            // [kSegWin]
+  int* first = reinterpret_cast<int*>(sk + kSegWin);      // [kSegWinPad]
+  int* last = first + kSegWinPad;                         // [kSegWinPad]
   __shared__ int sbuf[kSegThreads];
   const int t = threadIdx.x;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kSegTile;
@@ -494,28 +503,47 @@ __global__ void __launch_bounds__(kSegThreads)
     }
   }
   const int suf = block_excl_suffix_min(rrun, sbuf);
+  // final bounds packed as first | last << 16 (both < kSegWin < 2^16);
+  // `last` then holds the 32-bit second keys (below 2^sb <= 2^31) that the
+  // ranking loop reads four at a time
 #pragma unroll
   for (int q = 0; q < kSegItems; ++q) {
     const int w = w0 + q;
     if (w < kSegWin) {
       const int l = min(last[w], suf);
-      last[w] = l > kSegWin - 1 ? kSegWin - 1 : l;
+      first[w] |= (l > kSegWin - 1 ? kSegWin - 1 : l) << 16;
+      last[w] = static_cast<int>(static_cast<uint32_t>(sk[w] & kmask));
     }
   }
   __syncthreads();
+  const uint32_t* k32 = reinterpret_cast<const uint32_t*>(last);
   // owned elements and the forward halo
   const int own0 = kSegHalo + 1, own1 = own0 + kSegTile;
   for (int w = own0 + t; w < kSegWin - 1; w += kSegThreads) {
     const int64_t x = wbase + w;
     if (x >= m) break;
-    const int f = first[w], l = last[w];
+    const int fl = first[w];
+    const int f = fl & 0xffff, l = fl >> 16;
     const bool small = f > 0 && l < kSegWin - 1 && l - f + 1 <= kSegHalo;
     if (w < own1) large[x] = small ? 0 : 1;
     if (!small || f < own0 || f >= own1) continue;  // another block's group
-    const uint64_t kw = sk[w] & kmask;
+    // rank in the group by (second key, list position)
+    const uint32_t kw = k32[w];
     int rank = 0;
-    for (int u = f; u <= l; ++u) {
-      const uint64_t ku = sk[u] & kmask;
+    int u = f;
+    for (; u <= l && (u & 3); ++u) {
+      const uint32_t ku = k32[u];
+      rank += (ku < kw) || (ku == kw && u < w);
+    }
+    for (; u + 3 <= l; u += 4) {
+      const uint4 q4 = *reinterpret_cast<const uint4*>(k32 + u);
+      rank += (q4.x < kw) || (q4.x == kw && u < w);
+      rank += (q4.y < kw) || (q4.y == kw && u + 1 < w);
+      rank += (q4.z < kw) || (q4.z == kw && u + 2 < w);
+      rank += (q4.w < kw) || (q4.w == kw && u + 3 < w);
+    }
+    for (; u <= l; ++u) {
+      const uint32_t ku = k32[u];
       rank += (ku < kw) || (ku == kw && u < w);
     }
     const int64_t pos = wbase + f + rank;
@@ -790,8 +818,7 @@ int read_device_i64(const int64_t* dev, int64_t* out, cudaStream_t st) {
 static int segmented_sort(SaWorkspace& w, int64_t m, int sb, int bits,
                           CountSlot& slot, cudaStream_t st) {
   const int nseg = static_cast<int>((m + kSegTile - 1) / kSegTile);
-  const size_t seg_smem = static_cast<size_t>(kSegWin) * 16;
-  seg_local_kernel<<<nseg, kSegThreads, seg_smem, st>>>(
+  seg_local_kernel<<<nseg, kSegThreads, kSegSmem, st>>>(
       w.K[0], w.V[0], m, sb, w.K[1], w.V[1], w.flag);
   const bool small = small_tiles(m);
   const int nblk = static_cast<int>((m + elems_per_block(m) - 1) /
