@@ -220,6 +220,75 @@ __global__ void make_keys_kernel(const uint32_t* __restrict__ act,
   vals[t] = static_cast<uint32_t>(i);
 }
 
+// Dense token ids for the two-token pass. After the first-token sort,
+// block b counts the heads (first element of each run of equal tokens) of
+// its elements; blk_max is zeroed so that round_scan_blocks_kernel serves.
+template <int ITEMS>
+__global__ void __launch_bounds__(kScanThreads)
+    dense_count_kernel(const uint64_t* __restrict__ K, int64_t m,
+                       uint32_t* __restrict__ blk_max,
+                       uint32_t* __restrict__ blk_sum) {
+  __shared__ uint32_t ss[kSortWarps];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanThreads * ITEMS;
+  uint32_t sum = 0;
+  for (int r = 0; r < ITEMS; ++r) {
+    const int64_t t = base + r * kScanThreads + threadIdx.x;
+    if (t < m) sum += (t == 0 || K[t] != K[t - 1]) ? 1u : 0u;
+  }
+  sum = __reduce_add_sync(SG_FULL_MASK, sum);
+  if (lane_id() == 0) ss[warp_id()] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t b = 0;
+    for (int w = 0; w < kSortWarps; ++w) b += ss[w];
+    blk_max[blockIdx.x] = 0;
+    blk_sum[blockIdx.x] = b;
+  }
+}
+
+// dense[V[t]] = number of distinct tokens below K[t]: the order-preserving
+// id of position V[t]'s token among the D distinct ones (0 .. D - 1).
+template <int ITEMS>
+__global__ void __launch_bounds__(kScanThreads)
+    dense_write_kernel(const uint64_t* __restrict__ K,
+                       const uint32_t* __restrict__ V, int64_t m,
+                       const uint32_t* __restrict__ blk_sum,
+                       uint32_t* __restrict__ dense) {
+  __shared__ uint32_t ws[kSortWarps];
+  const int lane = lane_id(), warp = warp_id();
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanThreads * ITEMS;
+  uint32_t carry = blk_sum[blockIdx.x];
+  for (int r = 0; r < ITEMS; ++r) {
+    const int64_t t = base + r * kScanThreads + threadIdx.x;
+    const bool head = t < m && (t == 0 || K[t] != K[t - 1]);
+    const unsigned bal = __ballot_sync(SG_FULL_MASK, head);
+    if (lane == 0) ws[warp] = __popc(bal);
+    __syncthreads();
+    uint32_t pre = carry, tot = carry;
+    for (int w = 0; w < kSortWarps; ++w) {
+      if (w < warp) pre += ws[w];
+      tot += ws[w];
+    }
+    if (t < m) dense[V[t]] = pre + __popc(bal & ((2u << lane) - 1u)) - 1u;
+    carry = tot;
+    __syncthreads();
+  }
+}
+
+// Keys of the two-token pass: (dense[i] << B) | (dense[i+1] + 1, or 0 at
+// the end of the string), value i.
+__global__ void make2_keys_kernel(const uint32_t* __restrict__ dense,
+                                  int64_t n, int B,
+                                  uint64_t* __restrict__ keys,
+                                  uint32_t* __restrict__ vals) {
+  const int64_t i =
+      static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint64_t second = i + 1 < n ? static_cast<uint64_t>(dense[i + 1]) + 1 : 0;
+  keys[i] = (static_cast<uint64_t>(dense[i]) << B) | second;
+  vals[i] = static_cast<uint32_t>(i);
+}
+
 // Element t of the sorted active list: head of a new group? still tied?
 __device__ __forceinline__ void round_flags(const uint64_t* K, int64_t m,
                                             int64_t t, bool& head,
@@ -812,6 +881,30 @@ int read_device_i64(const int64_t* dev, int64_t* out, cudaStream_t st) {
   return read_count(dev, out, slot, st);
 }
 
+// Dense ids of the first-token sort (K[kcur], V[kcur]; n elements) into
+// w.rank; returns the number D of distinct tokens through *d (host sync).
+static int dense_ids(SaWorkspace& w, int kcur, int64_t n, CountSlot& slot,
+                     cudaStream_t st, int64_t* d) {
+  const bool small = small_tiles(n);
+  const int nblk = static_cast<int>((n + elems_per_block(n) - 1) /
+                                    elems_per_block(n));
+  if (small)
+    dense_count_kernel<kItemsSmall><<<nblk, kScanThreads, 0, st>>>(
+        w.K[kcur], n, w.blk_max, w.blk_sum);
+  else
+    dense_count_kernel<kScanItems><<<nblk, kScanThreads, 0, st>>>(
+        w.K[kcur], n, w.blk_max, w.blk_sum);
+  round_scan_blocks_kernel<<<1, 1024, 0, st>>>(w.blk_max, w.blk_sum, nblk,
+                                               w.m_dev);
+  if (small)
+    dense_write_kernel<kItemsSmall><<<nblk, kScanThreads, 0, st>>>(
+        w.K[kcur], w.V[kcur], n, w.blk_sum, w.rank);
+  else
+    dense_write_kernel<kScanItems><<<nblk, kScanThreads, 0, st>>>(
+        w.K[kcur], w.V[kcur], n, w.blk_sum, w.rank);
+  return read_count(w.m_dev, d, slot, st);
+}
+
 // Orders the active list (K[0], V[0]; m elements, grouped) by
 // (group, second key) into (K[1], V[1]): small groups on chip, large ones
 // through the global radix sort.
@@ -920,13 +1013,34 @@ extern "C" int sg_build_suffix_array(const int32_t* tokens, int64_t n,
   int err = SG_OK;
   int64_t m = 0;
   int acur = 0;
-  if (!apply_round(w, kcur, nullptr, w.act[acur], n, sa_out, slot, st, &m,
-                   &err))
-    return err;
+  int rounds = 0;
+  // Two-token pass in place of the first doubling round: with the D
+  // distinct tokens renumbered 0 .. D - 1 in order, a suffix's first two
+  // tokens pack into 2 * bitlen(D) <= 62 bits, and one sort of all n
+  // suffixes by them leaves the same groups and ranks as that round (whose
+  // active list, on copy-heavy text, is most of the corpus) at the price of
+  // ceil(2 * bitlen(D) / 8) digit passes.
+  int64_t n_distinct = 0;
+  int rc0 = dense_ids(w, kcur, n, slot, st, &n_distinct);
+  if (rc0 != SG_OK) return rc0;
+  if (n_distinct == n) {
+    // every first token differs: sorted already, no common prefixes
+    if (!apply_round(w, kcur, nullptr, w.act[acur], n, sa_out, slot, st, &m,
+                     &err))
+      return err;
+  } else {
+    const int B = bitlen(static_cast<uint64_t>(n_distinct));  // ids + 1 <= D
+    make2_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0,
+                        st>>>(w.rank, n, B, w.K[0], w.V[0]);
+    kcur = radix_sort(w, 0, n, 2 * B, st);
+    if (!apply_round(w, kcur, nullptr, w.act[acur], n, sa_out, slot, st, &m,
+                     &err))
+      return err;
+    rounds = 1;
+  }
   const int sb = bitlen(static_cast<uint64_t>(n));        // rank[i+h]+1 <= n
   const int pb = bitlen(static_cast<uint64_t>(n - 1));    // group start < n
-  int rounds = 0;
-  for (int64_t h = 1; m > 0; h <<= 1) {
+  for (int64_t h = 2; m > 0; h <<= 1) {
     if (h >= n) return SG_ERR_CUDA;  // cannot happen for a correct build
     make_keys_kernel<<<static_cast<unsigned>((m + 255) / 256), 256, 0, st>>>(
         w.act[acur], sa_out, w.rank, n, m, h, sb, w.K[0], w.V[0]);
