@@ -167,10 +167,12 @@ constexpr int kSCG = 8;      // CTAs per row of the backoff cluster kernel
 constexpr int kSMaxCols = 4; // pattern columns per lane (width <= 128)
 
 // _cmp_pattern with lane j holding pattern column j + 32 k in pc[k]
-// (columns >= lim are ignored). Warp-uniform result.
+// (columns >= lim are ignored). Warp-uniform result. Positions are below
+// n < 2^31 - 1, so index arithmetic is 32-bit (the search is bound by
+// instruction issue: thousands of warps probe at once).
 template <int NC>
 __device__ __forceinline__ int warp_cmp(const int32_t* __restrict__ corpus,
-                                        int64_t n, int64_t pos,
+                                        uint32_t n, uint32_t pos,
                                         const int (&pc)[NC], int lim,
                                         int64_t plen, int M) {
   const int lane = lane_id();
@@ -180,7 +182,7 @@ __device__ __forceinline__ int warp_cmp(const int32_t* __restrict__ corpus,
     const int j = lane + 32 * k;
     tok[k] = 0;
     if (j < lim) {
-      const int64_t x = pos + j;
+      const uint32_t x = pos + static_cast<uint32_t>(j);
       tok[k] = x < n ? corpus[x] : -1;
     }
   }
@@ -197,7 +199,7 @@ __device__ __forceinline__ int warp_cmp(const int32_t* __restrict__ corpus,
   }
   if (plen <= M) return 0;  // every column up to min(plen, M) matched
   // plen > M: the token at column M against pattern column M - 1
-  const int64_t x = pos + M;
+  const uint32_t x = pos + static_cast<uint32_t>(M);
   const int tv = x < n ? corpus[x] : -1;
   int src = 0;
 #pragma unroll
@@ -208,23 +210,21 @@ __device__ __forceinline__ int warp_cmp(const int32_t* __restrict__ corpus,
 }
 
 template <int NC>
-__device__ int64_t warp_bound(const int32_t* __restrict__ sa,
-                              const int32_t* __restrict__ corpus, int64_t n,
-                              int iters, const int (&pc)[NC], int M,
-                              int64_t plen, bool upper) {
+__device__ __forceinline__ int64_t warp_bound_cols(const int32_t* __restrict__ sa,
+                                   const int32_t* __restrict__ corpus,
+                                   uint32_t n, int iters, const int (&pc)[NC],
+                                   int M, int lim, int64_t plen, bool upper) {
   const int lane = lane_id();
-  const int lim = plen < M ? (plen > 0 ? static_cast<int>(plen) : 0) : M;
-  int64_t lo = 0, hi = n;
-  int64_t base = -1;  // once >= 0: lane i holds sa[base + i]
+  uint32_t lo = 0, hi = n;
+  int base = -1;  // once >= 0: lane i holds sa[base + i]
   int held = 0;
   for (int it = 0; it < iters; ++it) {
-    int64_t mid = (lo + hi) >> 1;
+    uint32_t mid = (lo + hi) >> 1;
     if (mid > n - 1) mid = n - 1;
-    int pos;
-    if (base >= 0)
-      pos = __shfl_sync(SG_FULL_MASK, held, static_cast<int>(mid - base));
-    else
-      pos = sa[mid];
+    const uint32_t pos = base >= 0
+        ? static_cast<uint32_t>(
+              __shfl_sync(SG_FULL_MASK, held, static_cast<int>(mid) - base))
+        : static_cast<uint32_t>(sa[mid]);
     const int c = warp_cmp<NC>(corpus, n, pos, pc, lim, plen, M);
     if (c < 0 || (upper && c == 0)) {
       lo = mid + 1;
@@ -235,17 +235,34 @@ __device__ int64_t warp_bound(const int32_t* __restrict__ sa,
       // From state (lo, hi) every later midpoint lies in [min, max(lo, hi)]
       // (hi never grows, lo never exceeds the old max + 1): cache that
       // window once it spans at most 32 entries.
-      const int64_t a = lo < hi ? lo : hi;
-      const int64_t z = lo < hi ? hi : lo;
-      const int64_t bs = a < n - 1 ? a : n - 1;
+      const uint32_t a = lo < hi ? lo : hi;
+      const uint32_t z = lo < hi ? hi : lo;
+      const uint32_t bs = a < n - 1 ? a : n - 1;
       if (z - bs <= 31) {
-        base = bs;
-        const int64_t x = bs + lane;
+        base = static_cast<int>(bs);
+        const uint32_t x = bs + static_cast<uint32_t>(lane);
         held = x < n ? sa[x] : 0;
       }
     }
   }
   return lo;
+}
+
+// One bound; patterns of at most 32 compared columns take the one-column
+// path (half of the backoff lengths for 64-token tails).
+template <int NC>
+__device__ __forceinline__ int64_t warp_bound(
+    const int32_t* __restrict__ sa, const int32_t* __restrict__ corpus,
+    int64_t n, int iters, const int (&pc)[NC], int M, int64_t plen,
+    bool upper) {
+  const int lim = plen < M ? (plen > 0 ? static_cast<int>(plen) : 0) : M;
+  const uint32_t un = static_cast<uint32_t>(n);
+  if (NC > 1 && lim <= 32 && plen <= M) {
+    const int pc1[1] = {pc[0]};
+    return warp_bound_cols<1>(sa, corpus, un, iters, pc1, M, lim, plen,
+                              upper);
+  }
+  return warp_bound_cols<NC>(sa, corpus, un, iters, pc, M, lim, plen, upper);
 }
 
 // search_interval: one warp per (pattern row, bound).
