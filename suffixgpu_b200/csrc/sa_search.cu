@@ -9,14 +9,12 @@
 // -1, pattern positions past its length always match), so the bounds are
 // identical to the reference's for any SA.
 //
-// One warp runs one bound: lane j holds pattern column j (and j + 32, ...),
-// so a probe reads the suffix's columns with one coalesced load and finds
-// the first mismatch with a ballot. The loop is a chain of dependent
-// memory round trips (SA entry, then its tokens); once every remaining
-// midpoint lies within 32 consecutive SA entries the warp loads those into
-// its lanes, and the remaining probes read only tokens. The backoff variant
+// One warp runs both bounds of a pattern: lane j holds pattern column j
+// (and j + 32, ...), so a probe reads the suffix's columns with one
+// coalesced load and finds the first mismatch with a ballot; the two
+// bounds share their probes until one compares equal. The backoff variant
 // searches every suffix length 1..M of each row's tail on one cluster of 8
-// CTAs (one warp per length and bound); CTA 0 gathers the intervals through
+// CTAs (one warp per length); CTA 0 gathers the intervals through
 // distributed shared memory and keeps, per cap, the longest found length
 // <= cap. Patterns wider than 128 columns use one thread per bound.
 #include <cooperative_groups.h>
@@ -166,17 +164,18 @@ constexpr int kSWarps = 8;   // warps per block of the search_interval kernel
 constexpr int kSCG = 8;      // CTAs per row of the backoff cluster kernel
 constexpr int kSMaxCols = 4; // pattern columns per lane (width <= 128)
 
-// _cmp_pattern with lane j holding pattern column j + 32 k in pc[k]
-// (columns >= lim are ignored). Warp-uniform result. Positions are below
-// n < 2^31 - 1, so index arithmetic is 32-bit (the search is bound by
-// instruction issue: thousands of warps probe at once).
+// The columns of the suffix at corpus position pos that a probe compares:
+// lane j reads column j + 32 k into tok[k] (columns >= lim read 0; past
+// the corpus end -1); lane 0 also reads column M into tm when the pattern
+// is longer than its width M (the reference then compares that token).
+// Positions are below n < 2^31 - 1, so index arithmetic is 32-bit (the
+// search is bound by instruction issue: thousands of warps probe at once).
 template <int NC>
-__device__ __forceinline__ int warp_cmp(const int32_t* __restrict__ corpus,
-                                        uint32_t n, uint32_t pos,
-                                        const int (&pc)[NC], int lim,
-                                        int64_t plen, int M) {
+__device__ __forceinline__ void load_probe(const int32_t* __restrict__ corpus,
+                                           uint32_t n, uint32_t pos, int lim,
+                                           int64_t plen, int M, int (&tok)[NC],
+                                           int& tm) {
   const int lane = lane_id();
-  int tok[NC];
 #pragma unroll
   for (int k = 0; k < NC; ++k) {
     const int j = lane + 32 * k;
@@ -186,6 +185,20 @@ __device__ __forceinline__ int warp_cmp(const int32_t* __restrict__ corpus,
       tok[k] = x < n ? corpus[x] : -1;
     }
   }
+  tm = 0;
+  if (plen > M && lane == 0) {
+    const uint32_t x = pos + static_cast<uint32_t>(M);
+    tm = x < n ? corpus[x] : -1;
+  }
+}
+
+// _cmp_pattern on a loaded probe, with lane j holding pattern column
+// j + 32 k in pc[k] (columns >= lim are ignored). Warp-uniform result.
+template <int NC>
+__device__ __forceinline__ int cmp_probe(const int (&tok)[NC], int tm,
+                                         const int (&pc)[NC], int lim,
+                                         int64_t plen, int M) {
+  const int lane = lane_id();
 #pragma unroll
   for (int k = 0; k < NC; ++k) {
     const int j = lane + 32 * k;
@@ -199,8 +212,7 @@ __device__ __forceinline__ int warp_cmp(const int32_t* __restrict__ corpus,
   }
   if (plen <= M) return 0;  // every column up to min(plen, M) matched
   // plen > M: the token at column M against pattern column M - 1
-  const uint32_t x = pos + static_cast<uint32_t>(M);
-  const int tv = x < n ? corpus[x] : -1;
+  const int tv = __shfl_sync(SG_FULL_MASK, tm, 0);
   int src = 0;
 #pragma unroll
   for (int k = 0; k < NC; ++k)
@@ -209,63 +221,97 @@ __device__ __forceinline__ int warp_cmp(const int32_t* __restrict__ corpus,
   return tv < pv ? -1 : (tv > pv ? 1 : 0);
 }
 
-template <int NC>
-__device__ __forceinline__ int64_t warp_bound_cols(const int32_t* __restrict__ sa,
-                                   const int32_t* __restrict__ corpus,
-                                   uint32_t n, int iters, const int (&pc)[NC],
-                                   int M, int lim, int64_t plen, bool upper) {
-  const int lane = lane_id();
-  uint32_t lo = 0, hi = n;
-  int base = -1;  // once >= 0: lane i holds sa[base + i]
-  int held = 0;
-  for (int it = 0; it < iters; ++it) {
-    uint32_t mid = (lo + hi) >> 1;
-    if (mid > n - 1) mid = n - 1;
-    const uint32_t pos = base >= 0
-        ? static_cast<uint32_t>(
-              __shfl_sync(SG_FULL_MASK, held, static_cast<int>(mid) - base))
-        : static_cast<uint32_t>(sa[mid]);
-    const int c = warp_cmp<NC>(corpus, n, pos, pc, lim, plen, M);
-    if (c < 0 || (upper && c == 0)) {
-      lo = mid + 1;
-    } else {
-      hi = mid;
-    }
-    if (base < 0 && it + 1 < iters) {
-      // From state (lo, hi) every later midpoint lies in [min, max(lo, hi)]
-      // (hi never grows, lo never exceeds the old max + 1): cache that
-      // window once it spans at most 32 entries.
-      const uint32_t a = lo < hi ? lo : hi;
-      const uint32_t z = lo < hi ? hi : lo;
-      const uint32_t bs = a < n - 1 ? a : n - 1;
-      if (z - bs <= 31) {
-        base = static_cast<int>(bs);
-        const uint32_t x = bs + static_cast<uint32_t>(lane);
-        held = x < n ? sa[x] : 0;
-      }
-    }
-  }
-  return lo;
+__device__ __forceinline__ uint32_t sa_mid(uint32_t lo, uint32_t hi,
+                                           uint32_t n) {
+  const uint32_t m = (lo + hi) >> 1;
+  return m > n - 1 ? n - 1 : m;
 }
 
-// One bound; patterns of at most 32 compared columns take the one-column
+// Both bounds of one pattern (lower: first suffix with cmp >= 0, upper:
+// first with cmp > 0) by the reference's midpoint rule. The two searches
+// take the same steps until a probe compares equal, so they share those
+// probes; from there the lower bound continues below the equal probe and
+// the upper bound above it, both probes of a step loaded together. Once a
+// bound's range is empty every further step of the reference's fixed
+// ceil(log2(n + 1)) count leaves it unchanged, so its loop stops there.
+template <int NC>
+__device__ __forceinline__ void warp_bounds_cols(
+    const int32_t* __restrict__ sa, const int32_t* __restrict__ corpus,
+    uint32_t n, int iters, const int (&pc)[NC], int M, int lim, int64_t plen,
+    uint32_t& out_lo, uint32_t& out_hi) {
+  uint32_t lo = 0, hi = n;
+  int it = 0;
+  uint32_t eq = 0;
+  bool split = false;
+  for (; it < iters && lo < hi; ++it) {
+    const uint32_t mid = sa_mid(lo, hi, n);
+    int tok[NC], tm;
+    load_probe<NC>(corpus, n, static_cast<uint32_t>(sa[mid]), lim, plen, M,
+                   tok, tm);
+    const int c = cmp_probe<NC>(tok, tm, pc, lim, plen, M);
+    if (c < 0) {
+      lo = mid + 1;
+    } else if (c > 0) {
+      hi = mid;
+    } else {
+      eq = mid;
+      split = true;
+      ++it;
+      break;
+    }
+  }
+  if (!split) {
+    out_lo = out_hi = lo;
+    return;
+  }
+  uint32_t llo = lo, lhi = eq, ulo = eq + 1, uhi = hi;
+  for (; it < iters && (llo < lhi || ulo < uhi); ++it) {
+    const bool dl = llo < lhi, du = ulo < uhi;
+    const uint32_t ml = sa_mid(llo, lhi, n), mu = sa_mid(ulo, uhi, n);
+    // (a finished bound loads nothing: zero columns, no column M)
+    int tl[NC], tml, tu[NC], tmu;
+    load_probe<NC>(corpus, n, static_cast<uint32_t>(sa[ml]), dl ? lim : 0,
+                   dl ? plen : 0, M, tl, tml);
+    load_probe<NC>(corpus, n, static_cast<uint32_t>(sa[mu]), du ? lim : 0,
+                   du ? plen : 0, M, tu, tmu);
+    if (dl) {
+      if (cmp_probe<NC>(tl, tml, pc, lim, plen, M) < 0)
+        llo = ml + 1;
+      else
+        lhi = ml;
+    }
+    if (du) {
+      if (cmp_probe<NC>(tu, tmu, pc, lim, plen, M) <= 0)
+        ulo = mu + 1;
+      else
+        uhi = mu;
+    }
+  }
+  out_lo = llo;
+  out_hi = ulo;
+}
+
+// Both bounds; patterns of at most 32 compared columns take the one-column
 // path (half of the backoff lengths for 64-token tails).
 template <int NC>
-__device__ __forceinline__ int64_t warp_bound(
+__device__ __forceinline__ void warp_bounds(
     const int32_t* __restrict__ sa, const int32_t* __restrict__ corpus,
     int64_t n, int iters, const int (&pc)[NC], int M, int64_t plen,
-    bool upper) {
+    int64_t& lower, int64_t& upper) {
   const int lim = plen < M ? (plen > 0 ? static_cast<int>(plen) : 0) : M;
   const uint32_t un = static_cast<uint32_t>(n);
+  uint32_t a, b;
   if (NC > 1 && lim <= 32 && plen <= M) {
     const int pc1[1] = {pc[0]};
-    return warp_bound_cols<1>(sa, corpus, un, iters, pc1, M, lim, plen,
-                              upper);
+    warp_bounds_cols<1>(sa, corpus, un, iters, pc1, M, lim, plen, a, b);
+  } else {
+    warp_bounds_cols<NC>(sa, corpus, un, iters, pc, M, lim, plen, a, b);
   }
-  return warp_bound_cols<NC>(sa, corpus, un, iters, pc, M, lim, plen, upper);
+  lower = a;
+  upper = b;
 }
 
-// search_interval: one warp per (pattern row, bound).
+// search_interval: one warp per pattern row.
 template <int NC>
 __global__ void __launch_bounds__(kSWarps * 32)
     sa_search_warp_kernel(const int32_t* __restrict__ sa,
@@ -274,10 +320,8 @@ __global__ void __launch_bounds__(kSWarps * 32)
                           const int64_t* __restrict__ plen, int B, int iters,
                           int64_t* __restrict__ start,
                           int64_t* __restrict__ end) {
-  const int task = blockIdx.x * kSWarps + warp_id();
-  if (task >= 2 * B) return;  // warp-uniform
-  const int row = task >> 1;
-  const bool upper = task & 1;
+  const int row = blockIdx.x * kSWarps + warp_id();
+  if (row >= B) return;  // warp-uniform
   const int lane = lane_id();
   int pc[NC];
 #pragma unroll
@@ -285,14 +329,18 @@ __global__ void __launch_bounds__(kSWarps * 32)
     const int j = lane + 32 * k;
     pc[k] = j < M ? pat[static_cast<int64_t>(row) * M + j] : 0;
   }
-  const int64_t r = warp_bound<NC>(sa, corpus, n, iters, pc, M, plen[row], upper);
-  if (lane == 0) (upper ? end : start)[row] = r;
+  int64_t lo, hi;
+  warp_bounds<NC>(sa, corpus, n, iters, pc, M, plen[row], lo, hi);
+  if (lane == 0) {
+    start[row] = lo;
+    end[row] = hi;
+  }
 }
 
 // suffix_match_backoff: one cluster of kSCG CTAs per row, one warp per
-// (length, bound); CTA 0 gathers the intervals and selects per cap.
+// pattern length; CTA 0 gathers the intervals and selects per cap.
 template <int NC>
-__global__ void __cluster_dims__(kSCG, 1, 1) __launch_bounds__(1024)
+__global__ void __cluster_dims__(kSCG, 1, 1) __launch_bounds__(512)
     sa_backoff_cluster_kernel(const int32_t* __restrict__ sa,
                               const int32_t* __restrict__ corpus, int64_t n,
                               const int32_t* __restrict__ query, int Q,
@@ -303,8 +351,8 @@ __global__ void __cluster_dims__(kSCG, 1, 1) __launch_bounds__(1024)
                               int64_t* __restrict__ out_start,
                               int64_t* __restrict__ out_end) {
   cg::cluster_group cluster = cg::this_cluster();
-  __shared__ long long s_res[32];       // this CTA's bounds, one per warp
-  __shared__ long long s_all[2 * 128];  // CTA 0: every (length, bound)
+  __shared__ long long s_res[2 * 16];   // this CTA's intervals, one per warp
+  __shared__ long long s_all[2 * 128];  // CTA 0: every length's interval
   const int g = static_cast<int>(cluster.block_rank());
   const int b = blockIdx.x / kSCG;
   const int wpc = blockDim.x >> 5;
@@ -312,10 +360,9 @@ __global__ void __cluster_dims__(kSCG, 1, 1) __launch_bounds__(1024)
   const bool active = !row_mask || row_mask[b];
   const int64_t ql = qlen[b];
   const int task = g * wpc + warp;
-  if (task < 2 * M) {
-    const int l = (task >> 1) + 1;  // pattern length
-    const bool upper = task & 1;
-    int64_t r = 0;
+  if (task < M) {
+    const int l = task + 1;  // pattern length
+    int64_t lo = 0, hi = 0;
     if (active && l <= ql) {
       // pattern_l[j] = query[qlen - l + j] for j < l (the gather clamps
       // indices to the query width like the reference)
@@ -327,14 +374,20 @@ __global__ void __cluster_dims__(kSCG, 1, 1) __launch_bounds__(1024)
         const int64_t x = o + j;
         pc[k] = j < l ? query[static_cast<int64_t>(b) * Q + (x < Q ? x : Q - 1)] : 0;
       }
-      r = warp_bound<NC>(sa, corpus, n, iters, pc, M, l, upper);
+      warp_bounds<NC>(sa, corpus, n, iters, pc, M, l, lo, hi);
     }
-    if (lane == 0) s_res[warp] = r;
+    if (lane == 0) {
+      s_res[2 * warp] = lo;
+      s_res[2 * warp + 1] = hi;
+    }
   }
-  cluster.sync();  // every CTA's bounds are published
+  cluster.sync();  // every CTA's intervals are published
   if (g == 0) {
-    for (int i = threadIdx.x; i < 2 * M; i += blockDim.x)
-      s_all[i] = *cluster.map_shared_rank(&s_res[i % wpc], i / wpc);
+    for (int i = threadIdx.x; i < 2 * M; i += blockDim.x) {
+      const int t = i >> 1;  // length index
+      s_all[i] = *cluster.map_shared_rank(&s_res[2 * (t % wpc) + (i & 1)],
+                                          t / wpc);
+    }
   }
   cluster.sync();  // remote reads done; s_all visible to CTA 0
   if (g == 0) {
@@ -358,7 +411,7 @@ static int launch_search_warp(const int32_t* sa, const int32_t* corpus,
                               int64_t n, const int32_t* pattern, int batch,
                               int width, const int64_t* plen, int64_t* st,
                               int64_t* en, cudaStream_t stream) {
-  const int64_t blocks = (2 * static_cast<int64_t>(batch) + kSWarps - 1) / kSWarps;
+  const int64_t blocks = (static_cast<int64_t>(batch) + kSWarps - 1) / kSWarps;
   sa_search_warp_kernel<NC><<<static_cast<unsigned>(blocks), kSWarps * 32, 0,
                               stream>>>(sa, corpus, n, pattern, width, plen,
                                         batch, sa_iters(n), st, en);
@@ -373,7 +426,7 @@ static int launch_backoff_cluster(const int32_t* sa, const int32_t* corpus,
                                   const uint8_t* row_mask, int64_t* ol,
                                   int64_t* os, int64_t* oe,
                                   cudaStream_t stream) {
-  const int wpc = (2 * M + kSCG - 1) / kSCG;  // <= 32 for M <= 128
+  const int wpc = (M + kSCG - 1) / kSCG;  // <= 16 for M <= 128
   sa_backoff_cluster_kernel<NC><<<batch * kSCG, wpc * 32, 0, stream>>>(
       sa, corpus, n, query, qw, qlen, M, caps, C, row_mask, sa_iters(n), ol,
       os, oe);
