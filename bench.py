@@ -80,6 +80,9 @@ def parse():
     ap.add_argument("--global-warmup", type=int, default=8)
     ap.add_argument("--no-sharded", action="store_true",
                     help="skip the config 5 measurement in draft mode")
+    ap.add_argument("--sharded-log2-corpus", type=int, default=26,
+                    help="config 5 corpus and index capacity 2^k tokens "
+                         "(26 = the config; smaller for profiling captures)")
     ap.add_argument("--sharded-steps", type=int, default=512,
                     help="timed propose steps of config 5 per GPU")
     return ap.parse_args()
@@ -514,12 +517,15 @@ def run_sharded(args, dev, world: int, rank: int) -> dict | None:
     import torch.distributed as dist
     from suffixgpu_b200 import SuffixGPUDrafter
     from suffixgpu_b200 import workloads as wl
-    data = wl.config5(rank=rank, steps=DECODE5)
+    lg = min(26, max(16, args.sharded_log2_corpus))
+    data = wl.config5(rank=rank, steps=DECODE5, n_docs=1 << (lg - 10))
+    cfg = dict(wl.CONFIG5_DRAFTER)
+    cfg["global_capacity"] = 1 << lg
     if world > 1:
         from suffixgpu_b200.distributed import ShardedSuffixDrafter
-        d = ShardedSuffixDrafter(device=dev, **wl.CONFIG5_DRAFTER)
+        d = ShardedSuffixDrafter(device=dev, **cfg)
     else:
-        d = SuffixGPUDrafter(device=dev, **wl.CONFIG5_DRAFTER)
+        d = SuffixGPUDrafter(device=dev, **cfg)
     docs = torch.from_numpy(data["corpus_docs"]).to(dev)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
@@ -585,8 +591,8 @@ def run_sharded(args, dev, world: int, rank: int) -> dict | None:
             "corpus_tokens": int(d.global_index.active_len),
             "load_s": load_max,
             "workload": "config5: 128 rows x S=16384 per GPU, k=32, P=64, "
-                        "R=256, 8 backoff, factor 2.0, min_prob 0.1; 2^26-"
-                        "token corpus of 512 x 512 templates (5% "
+                        "R=256, 8 backoff, factor 2.0, min_prob 0.1; "
+                        f"2^{lg}-token corpus of 512 x 512 templates (5% "
                         "substitution, vocab 128256), index replicated on "
                         "every GPU",
             "l2": "16 rotating replicas x 8 MiB token buffer"}
