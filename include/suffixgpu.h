@@ -272,6 +272,23 @@ int sg_gather_tails(const int32_t* token_ids, int64_t row_stride,
                     int32_t pattern_len, int32_t* tails, int64_t* tail_len,
                     sg_stream_t stream);
 
+/* The tails sg_gather_tails would return after update_state
+ * (proposer.py:135-184) of these rows with these sampled ids (NULL: no
+ * update, counts = base_counts), read from the buffer before the scatter
+ * (it only reads positions the scatter leaves alone, so the local step may
+ * update the rows concurrently on another stream); row_mask[b] receives
+ * the drafting mask (propose_with_update: count > 0 and new count < limit;
+ * propose: mask[b], or 1 when mask is NULL). No reference counterpart:
+ * the reference gathers after the update (proposer.py:243-320). */
+int sg_gather_tails_update(const int32_t* token_ids, int64_t row_stride,
+                           int32_t seq_len, const int32_t* base_counts,
+                           const int32_t* sampled, int32_t sampled_cols,
+                           const int32_t* valid_count, int64_t limit,
+                           const uint8_t* mask, int32_t batch,
+                           int32_t pattern_len, int32_t* tails,
+                           int64_t* tail_len, uint8_t* row_mask,
+                           sg_stream_t stream);
+
 /* Tail of GlobalIndex._query_backoff (global_index.py:321-370) and
  * _gather_cont (:443-463): SA-vs-delta choice per cap, adjacent-duplicate
  * removal, strided SA interval sampling, continuation block cont

@@ -91,6 +91,10 @@ _SIGS: dict[str, list] = {
                                c_int32, c_int32, c_void_p, c_int32, c_void_p,
                                c_int32, c_int32, c_void_p, c_void_p,
                                c_void_p, c_void_p, c_void_p],
+    "sg_gather_tails_update": [c_void_p, c_int64, c_int32, c_void_p, c_void_p,
+                               c_int32, c_void_p, c_int64, c_void_p, c_int32,
+                               c_int32, c_void_p, c_void_p, c_void_p,
+                               c_void_p],
     "sg_gather_tails": [c_void_p, c_int64, c_int32, c_void_p, c_int32,
                         c_int32, c_void_p, c_void_p, c_void_p],
     "sg_global_candidates": [c_void_p, c_void_p, c_void_p, c_void_p,

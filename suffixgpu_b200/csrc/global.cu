@@ -49,6 +49,63 @@ __global__ void gather_tails_kernel(const int32_t* __restrict__ tok,
   }
 }
 
+// Tails of the rows as update_state will leave them (proposer.py:135-184,
+// 110-125), read from the buffer before the scatter: positions below the
+// row's count come from the buffer, the appended ones from the sampled ids
+// where the scatter writes them (j < count, id != -1, inside the row) and
+// from the buffer where it does not. The scatter never writes a position
+// this reads, so the local step can update the rows concurrently. Also
+// the row mask of propose_with_update (count > 0 and new count < limit).
+__global__ void gather_tails_update_kernel(
+    const int32_t* __restrict__ tok, int64_t stride, int S,
+    const int32_t* __restrict__ base_counts,
+    const int32_t* __restrict__ sampled, int T,
+    const int32_t* __restrict__ valid_count, int64_t limit,
+    const uint8_t* __restrict__ mask, int B, int P,
+    int32_t* __restrict__ tails, int64_t* __restrict__ tail_len,
+    uint8_t* __restrict__ row_mask) {
+  const int b = blockIdx.x;
+  __shared__ long long s_cnt;
+  const int32_t* srow =
+      sampled ? sampled + static_cast<int64_t>(b) * T : nullptr;
+  const int64_t base = base_counts[b];
+  if (threadIdx.x == 0) {
+    long long cnt = 0;
+    if (srow) {
+      if (valid_count) {
+        cnt = valid_count[b];
+      } else {
+        for (int j = 0; j < T; ++j) cnt += srow[j] != -1;
+      }
+    }
+    s_cnt = cnt;
+  }
+  __syncthreads();
+  const int64_t cnt = s_cnt;
+  const int64_t q = base + cnt;
+  const int64_t tl = q < P ? q : P;
+  const int32_t* row = tok + static_cast<int64_t>(b) * stride;
+  if (threadIdx.x == 0) {
+    tail_len[b] = tl;
+    row_mask[b] = srow ? static_cast<uint8_t>(cnt > 0 && q < limit)
+                       : static_cast<uint8_t>(mask ? mask[b] != 0 : 1);
+  }
+  for (int j = threadIdx.x; j < P; j += blockDim.x) {
+    int v = 0;
+    if (j < tl) {
+      int64_t idx = q - tl + j;
+      idx = idx < 0 ? 0 : (idx > S - 1 ? S - 1 : idx);
+      v = row[idx];
+      const int64_t u = idx - base;  // appended id index
+      if (srow && u >= 0 && u < cnt && u < T) {
+        const int sv = srow[u];
+        if (sv != -1) v = sv;  // idx < S: the scatter writes sv there
+      }
+    }
+    tails[static_cast<int64_t>(b) * P + j] = v;
+  }
+}
+
 struct GlobalCandArgs {
   const int64_t* sa_len;
   const int64_t* sa_start;
@@ -433,6 +490,26 @@ extern "C" int sg_gather_tails(const int32_t* token_ids, int64_t row_stride,
                         reinterpret_cast<cudaStream_t>(stream)>>>(
       token_ids, row_stride, seq_len, counts, batch, pattern_len, tails,
       tail_len);
+  return check_launch();
+}
+
+extern "C" int sg_gather_tails_update(
+    const int32_t* token_ids, int64_t row_stride, int32_t seq_len,
+    const int32_t* base_counts, const int32_t* sampled, int32_t sampled_cols,
+    const int32_t* valid_count, int64_t limit, const uint8_t* mask,
+    int32_t batch, int32_t pattern_len, int32_t* tails, int64_t* tail_len,
+    uint8_t* row_mask, sg_stream_t stream) {
+  if (batch < 0 || seq_len < 1 || row_stride < seq_len || pattern_len < 1 ||
+      (sampled && sampled_cols < 1))
+    return SG_ERR_INVALID;
+  if (batch == 0) return SG_OK;
+  if (!token_ids || !base_counts || !tails || !tail_len || !row_mask)
+    return SG_ERR_INVALID;
+  gather_tails_update_kernel<<<batch, 64, 0,
+                               reinterpret_cast<cudaStream_t>(stream)>>>(
+      token_ids, row_stride, seq_len, base_counts, sampled, sampled_cols,
+      valid_count, limit, mask, batch, pattern_len, tails, tail_len,
+      row_mask);
   return check_launch();
 }
 

@@ -157,6 +157,7 @@ class GlobalIndex:
         self._jobs: queue.SimpleQueue | None = None
         self.rebuilds = 0
         self.last_rounds = 0
+        self._step_bufs: dict = {}
         self._sa_ws: torch.Tensor | None = None
         # Incremental rebuilds (sg_suffix_array_append): the staging SA is
         # merged from the active one when at most half of the snapshot has
@@ -636,28 +637,97 @@ class GlobalIndex:
     # ------------------------------------------------------------------
     # drafter step (proposer.py:246-320)
     # ------------------------------------------------------------------
-    def propose_combine(self, counts: torch.Tensor, token_ids: torch.Tensor,
-                        local: dict, drafter) -> tuple[torch.Tensor,
-                                                       torch.Tensor]:
-        """Global candidates for the rows the local kernel just drafted,
-        expanded and scored, then combined with the local winner in place
-        (global wins only on a strictly greater score)."""
+    def start_global_step(self, drafter, counts: torch.Tensor,
+                          token_ids: torch.Tensor, sampled=None,
+                          valid_count=None, limit: int | None = None,
+                          mask=None, streams=None) -> dict:
+        """First half of the drafter's global step (proposer.py:243-304):
+        the rows' tails as update_state leaves them (read before the scatter,
+        sg_gather_tails_update), the SA backoff search and the delta scan.
+        Its buffers belong to the current stream. With streams =
+        (s0, s1, four events) the work forks off the current stream: tails
+        then the SA search on s0, the delta scan on s1 after the tails, so
+        both searches run while the local step (which performs the scatter)
+        runs on the current stream; finish_global_step joins them."""
         dev = self.device
         b, s = token_ids.shape
         p = drafter.max_pattern_len
-        counts = ops.as_i32(counts)
-        tails = torch.empty(b, p, dtype=torch.int32, device=dev)
-        tail_len = torch.empty(b, dtype=torch.int64, device=dev)
-        st = stream_of(dev)
-        call("sg_gather_tails", ptr(token_ids), token_ids.stride(0), s,
-             ptr(counts), b, p, ptr(tails), ptr(tail_len), st)
         caps = drafter._global_caps
+        cnum = caps.numel()
+        r = self.max_occurrences
+        counts = ops.as_i32(counts)
+        samp = None if sampled is None else ops.as_i32(sampled)
+        vc = None if (sampled is None or valid_count is None) \
+            else ops.as_i32(valid_count)
+        m8 = None if (sampled is not None or mask is None) \
+            else mask.to(torch.uint8).contiguous()
+        # Eager steps keep their buffers per shape (the fork waits for
+        # everything already queued on the current stream, the previous
+        # step's use of them included); a step being captured into a CUDA
+        # graph allocates its own from the graph's pool, so that replays
+        # never share them with eager calls on other streams.
+        capturing = torch.cuda.is_current_stream_capturing()
+        key = (b, p, cnum, r)
+        st = None if capturing else self._step_bufs.get(key)
+        if st is None:
+            i64 = dict(dtype=torch.int64, device=dev)
+            st = {"tails": torch.empty(b, p, dtype=torch.int32, device=dev),
+                  "tail_len": torch.empty(b, **i64),
+                  "row_mask": torch.empty(b, dtype=torch.uint8, device=dev),
+                  "found": [torch.empty(b, cnum, **i64) for _ in range(4)]}
+            st["found"].insert(4, torch.empty(b, cnum, r, **i64))
+            st["found"].append(torch.empty(b, cnum, **i64))
+            if not capturing:
+                self._step_bufs[key] = st
+        sa_len, sa_start, sa_end, d_len, d_pos, d_cnt = st["found"]
+        tails, tail_len, row_mask = st["tails"], st["tail_len"], st["row_mask"]
+        if streams is None:
+            s_tails = s_sa = s_delta = stream_of(dev)
+        else:
+            s0, s1, ev = streams
+            ev[0].record(torch.cuda.current_stream(dev))
+            s0.wait_event(ev[0])
+            s_tails = s_sa = s0.cuda_stream
+            s_delta = s1.cuda_stream
+        call("sg_gather_tails_update", ptr(token_ids), token_ids.stride(0), s,
+             ptr(counts), ptr(samp), 0 if samp is None else samp.shape[1],
+             ptr(vc), s if limit is None else int(limit), ptr(m8), b, p,
+             ptr(tails), ptr(tail_len), ptr(row_mask), s_tails)
+        if streams is not None:
+            ev[1].record(s0)  # the delta scan needs the tails
+            s1.wait_event(ev[1])
+        call("sg_suffix_match_backoff", ptr(self.sa), ptr(self.corpus),
+             self.capacity, ptr(tails), b, p, ptr(tail_len), p, ptr(caps),
+             cnum, ptr(row_mask), ptr(sa_len), ptr(sa_start), ptr(sa_end),
+             s_sa)
+        call("sg_delta_match_backoff", ptr(self.delta), self.delta_capacity,
+             ptr(self.delta_len_t), ptr(tails), b, p, ptr(tail_len), p,
+             ptr(caps), cnum, r, ptr(row_mask), ptr(d_len), ptr(d_pos),
+             ptr(d_cnt), s_delta)
+        return st
+
+    def finish_global_step(self, pending: dict, local: dict, drafter,
+                           streams=None) -> tuple[torch.Tensor, torch.Tensor]:
+        """Second half: joins the searches, then global candidates expanded
+        and scored and combined with the local winner in place (global wins
+        only on a strictly greater score; proposer.py:305-320)."""
+        dev = self.device
+        if streams is not None:
+            s0, s1, ev = streams
+            cur = torch.cuda.current_stream(dev)
+            ev[2].record(s0)
+            ev[3].record(s1)
+            cur.wait_event(ev[2])
+            cur.wait_event(ev[3])
+        found = pending["found"]
+        row_mask = pending["row_mask"]
+        b = row_mask.shape[0]
+        caps = drafter._global_caps
+        cnum = caps.numel()
         spec = (drafter.max_spec_factor is not None,
                 drafter.max_spec_factor or 0.0, drafter.max_spec_offset)
-        row_mask = local["row_mask"]
-        cnum = caps.numel()
-        found = self._searches(tails, tail_len, p, caps, row_mask)
         draft, nv = local["draft"], local["num_valid"]
+        st = stream_of(dev)
         # fused candidates + expand + selection (continuations on chip);
         # the continuation width must be the draft length
         st_code = _UNSUPPORTED if self.k != drafter.k else lib().sg_global_draft(
@@ -683,3 +753,13 @@ class GlobalIndex:
              ptr(local["best_score"]), ptr(row_mask), ptr(chain), ptr(emit),
              ptr(score), b, cnum, drafter.k, st)
         return draft, nv
+
+    def propose_combine(self, counts: torch.Tensor, token_ids: torch.Tensor,
+                        local: dict, drafter) -> tuple[torch.Tensor,
+                                                       torch.Tensor]:
+        """Global candidates for the rows the local kernel just drafted (and
+        updated), expanded, scored and combined with the local winner, on
+        the current stream."""
+        pend = self.start_global_step(drafter, counts, token_ids,
+                                      mask=local["row_mask"])
+        return self.finish_global_step(pend, local, drafter)

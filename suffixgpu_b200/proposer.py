@@ -64,6 +64,7 @@ class SuffixGPUDrafter:
         self.num_backoff = max(1, int(num_backoff))
         self.vote_smoothing_alpha = float(vote_smoothing_alpha)
         self.parallel_paths = bool(parallel_paths)
+        self._aux = None
         support_thresholds = tuple(2 ** i for i in range(self.num_backoff))
         caps = global_caps(max_pattern_len, self.num_backoff)
         self._global_caps = torch.tensor(caps, dtype=torch.int64,
@@ -121,11 +122,20 @@ class SuffixGPUDrafter:
                 sampled=sampled_token_ids,
                 valid_count=valid_sampled_tokens_count, limit=limit)
             return o["draft"], o["num_valid"], o["new_counts"]
+        # the global searches fork off before the local step (they read the
+        # rows' tails as the local step's scatter will leave them)
+        streams = self._aux_streams()
+        pend = self.global_index.start_global_step(
+            self, num_tokens_no_spec, token_ids_gpu,
+            sampled=sampled_token_ids,
+            valid_count=valid_sampled_tokens_count, limit=limit,
+            streams=streams)
         o = self.local_kernel.run(
             num_tokens_no_spec, token_ids_gpu, sampled=sampled_token_ids,
             valid_count=valid_sampled_tokens_count, limit=limit,
             extras=True)
-        draft, nv = self._global_step(o["new_counts"], token_ids_gpu, o)
+        draft, nv = self.global_index.finish_global_step(pend, o, self,
+                                                         streams)
         return draft, nv, o["new_counts"]
 
     def propose(self, num_tokens_no_spec: torch.Tensor,
@@ -139,13 +149,26 @@ class SuffixGPUDrafter:
             o = self.local_kernel.run(num_tokens_no_spec, token_ids_gpu,
                                       mask=combined_mask)
             return o["draft"], o["num_valid"]
+        streams = self._aux_streams()
+        pend = self.global_index.start_global_step(
+            self, num_tokens_no_spec, token_ids_gpu, mask=combined_mask,
+            streams=streams)
         o = self.local_kernel.run(num_tokens_no_spec, token_ids_gpu,
                                   mask=combined_mask, extras=True)
-        return self._global_step(num_tokens_no_spec, token_ids_gpu, o)
+        return self.global_index.finish_global_step(pend, o, self, streams)
 
-    def _global_step(self, counts, token_ids, local):
-        return self.global_index.propose_combine(
-            counts, token_ids, local, self)
+    def _aux_streams(self):
+        """The two side streams of the global searches and the four events
+        of their fork and join (the reference's parallel_paths, proposer.py:
+        243-320), created on first use and reused; None runs everything on
+        the current stream."""
+        if not self.parallel_paths:
+            return None
+        if self._aux is None:
+            self._aux = (torch.cuda.Stream(self.device),
+                         torch.cuda.Stream(self.device),
+                         tuple(torch.cuda.Event() for _ in range(4)))
+        return self._aux
 
     # ------------------------------------------------------------------
     # host-side ingestion (proposer.py:329-390)
