@@ -87,6 +87,11 @@ def test_invalid_arguments_rejected_without_gpu(libpath):
     assert r.value == 0
     assert L.sg_suffix_array_append_workspace_size(1 << 20) >= \
         L.sg_suffix_array_workspace_size(1 << 20)
+    # tails before the update: bad shapes, and an empty batch
+    assert L.sg_gather_tails_update(None, 4, 8, None, None, 0, None, 8, None,
+                                    2, 4, None, None, None, None) == 1
+    assert L.sg_gather_tails_update(None, 8, 8, None, None, 0, None, 8, None,
+                                    0, 4, None, None, None, None) == 0
 
 
 def test_torch_operator_registers():

@@ -497,3 +497,59 @@ def test_state_dict_round_trip():
     g.append_documents(more)
     h.append_documents(more)
     assert torch.equal(g.corpus, h.corpus) and torch.equal(g.sa, h.sa)
+
+
+def test_tails_before_update_match_tails_after():
+    """sg_gather_tails_update (tails read before the scatter, for the
+    forked global searches) equals the scatter followed by the plain tail
+    gather, with the drafting mask of propose_with_update / propose: -1
+    sampled ids, explicit and implicit valid counts, rows that reach or pass
+    the row end or the limit, and rows with an empty history."""
+    from suffixgpu_b200 import ops
+    from suffixgpu_b200._lib import call, ptr
+    rng = np.random.default_rng(21)
+    b, s, t, p = 40, 96, 6, 32
+    tok = rng.integers(0, 50, size=(b, s)).astype(np.int32)
+    base = rng.integers(0, s + 3, size=b).astype(np.int32)
+    base[:4] = [0, 1, s - 1, s]
+    samp = rng.integers(0, 50, size=(b, t)).astype(np.int32)
+    samp[rng.random((b, t)) < 0.3] = -1
+    for explicit in (False, True):
+        vc = rng.integers(0, t + 1, size=b).astype(np.int32) if explicit \
+            else None
+        limit = s - 5
+        # (device copies held in names: a pointer taken from a temporary
+        # would outlive its memory)
+        d_tok, d_base, d_samp = _dev(tok), _dev(base), _dev(samp)
+        d_vc = None if vc is None else _dev(vc)
+        tails = torch.empty(b, p, dtype=torch.int32, device=DEV)
+        tlen = torch.empty(b, dtype=torch.int64, device=DEV)
+        mask = torch.empty(b, dtype=torch.uint8, device=DEV)
+        call("sg_gather_tails_update", ptr(d_tok), s, s, ptr(d_base),
+             ptr(d_samp), t, ptr(d_vc), limit, ptr(None), b, p, ptr(tails),
+             ptr(tlen), ptr(mask), torch.cuda.current_stream().cuda_stream)
+        # reference: the scatter, then the tails of the updated rows
+        upd = _dev(tok)
+        new = ops.scatter_append(upd, d_base, d_vc, d_samp)
+        exp_t = torch.empty(b, p, dtype=torch.int32, device=DEV)
+        exp_l = torch.empty(b, dtype=torch.int64, device=DEV)
+        call("sg_gather_tails", ptr(upd), s, s, ptr(new), b, p, ptr(exp_t),
+             ptr(exp_l), torch.cuda.current_stream().cuda_stream)
+        cnt = (samp != -1).sum(1) if vc is None else vc
+        exp_m = (cnt > 0) & (_host(new) < limit)
+        np.testing.assert_array_equal(_host(tlen), _host(exp_l))
+        np.testing.assert_array_equal(_host(mask).astype(bool), exp_m)
+        # the tails of rows that draft are what the searches read
+        np.testing.assert_array_equal(_host(tails)[exp_m], _host(exp_t)[exp_m])
+        # the buffer was not touched
+        np.testing.assert_array_equal(_host(d_tok), tok)
+    # propose (no update): tails of the rows as they are, the given mask
+    m = (rng.random(b) < 0.7)
+    d_tok, d_base, d_m = _dev(tok), _dev(base), _dev(m.astype(np.uint8))
+    call("sg_gather_tails_update", ptr(d_tok), s, s, ptr(d_base), ptr(None),
+         0, ptr(None), s, ptr(d_m), b, p, ptr(tails), ptr(tlen), ptr(mask),
+         torch.cuda.current_stream().cuda_stream)
+    call("sg_gather_tails", ptr(d_tok), s, s, ptr(d_base), b, p, ptr(exp_t),
+         ptr(exp_l), torch.cuda.current_stream().cuda_stream)
+    np.testing.assert_array_equal(_host(tails), _host(exp_t))
+    np.testing.assert_array_equal(_host(mask).astype(bool), m)
