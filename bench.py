@@ -28,6 +28,11 @@ import time
 
 import numpy as np
 
+# Rank 0 prints exactly one JSON line on stdout; NCCL's version banner
+# (NCCL_DEBUG=VERSION) would print another one there.
+if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+    os.environ["NCCL_DEBUG"] = "WARN"
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
