@@ -41,6 +41,15 @@ const char* sg_status_string(int status);
 int sg_last_cuda_error(void);
 /* ABI version: (major << 16) | minor. */
 int sg_abi_version(void);
+/* Device address of page-locked ("pinned") host memory: SG_OK and
+ * *device_ptr set when host_ptr lies in a cudaHostAlloc / cudaHostRegister
+ * allocation the current device can reach; SG_ERR_INVALID for pageable or
+ * device memory. With unified addressing the two addresses are equal. The
+ * local draft step accepts such addresses for its sampled ids and its
+ * draft / num_valid outputs (see sg_local_inputs). No reference counterpart:
+ * the reference takes device tensors only; this lets a host-side caller
+ * skip the separate copies of the step's small inputs and outputs. */
+int sg_mapped_host_ptr(const void* host_ptr, void** device_ptr);
 
 /* ---- local drafter ------------------------------------------------------
  * Drafter parameters shared by the local and global paths
@@ -62,7 +71,12 @@ typedef struct sg_draft_params {
   float vote_alpha;         /* vote_smoothing_alpha (rounded to fp32) */
 } sg_draft_params;
 
-/* Inputs of one local draft step. */
+/* Inputs of one local draft step. `sampled`, `valid_count` and the
+ * outputs `draft` / `num_valid` may also point into page-locked host memory
+ * (the address sg_mapped_host_ptr returns): the kernel then reads the ids
+ * and writes the drafts over the host link itself, so a host-driven decode
+ * loop needs no separate host<->device copies for them. The caller must not
+ * touch those host buffers until the stream has passed the call. */
 typedef struct sg_local_inputs {
   const int32_t* num_tokens; /* [B] counts before the update (propose mode:
                                 the current counts) */

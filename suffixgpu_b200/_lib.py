@@ -65,6 +65,7 @@ class LocalOutputs(Structure):
 _SIGS: dict[str, list] = {
     "sg_local_draft": [POINTER(DraftParams), POINTER(LocalInputs),
                        POINTER(LocalOutputs), c_void_p],
+    "sg_mapped_host_ptr": [c_void_p, POINTER(c_void_p)],
     "sg_scatter_append": [c_void_p, c_int64, c_int32, c_int32, c_void_p,
                           c_void_p, c_void_p, c_int32, c_void_p, c_void_p],
     "sg_match_back": [c_void_p, c_int64, c_int64, c_void_p, c_int32, c_int32,

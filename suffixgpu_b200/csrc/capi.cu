@@ -45,4 +45,22 @@ extern "C" const char* sg_status_string(int status) {
 
 extern "C" int sg_last_cuda_error(void) { return sg::g_last_cuda_error; }
 
-extern "C" int sg_abi_version(void) { return (1 << 16) | 0; }
+extern "C" int sg_abi_version(void) { return (1 << 16) | 1; }
+
+extern "C" int sg_mapped_host_ptr(const void* host_ptr, void** device_ptr) {
+  if (!host_ptr || !device_ptr) return SG_ERR_INVALID;
+  *device_ptr = nullptr;
+  cudaPointerAttributes attr{};
+  const cudaError_t e = cudaPointerGetAttributes(&attr, host_ptr);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // a failed query leaves no sticky error behind
+    sg::set_cuda_error(e);
+    return SG_ERR_INVALID;
+  }
+  // page-locked host memory mapped into the device's address space; plain
+  // pageable memory reports cudaMemoryTypeUnregistered and is refused
+  if (attr.type != cudaMemoryTypeHost || attr.devicePointer == nullptr)
+    return SG_ERR_INVALID;
+  *device_ptr = attr.devicePointer;
+  return SG_OK;
+}

@@ -7,6 +7,10 @@
 // current torch stream. The drafter's settings arrive as a small host
 // tensor holding an sg_draft_params struct; the batch shape comes from
 // token_ids. Errors raise (TORCH_CHECK) with the library's status string.
+// The sampled ids (and valid counts) may be page-locked host tensors and
+// the draft / num_valid outputs may be caller-provided tensors, on the
+// device or in page-locked host memory: the kernel then reads and writes
+// those host buffers directly, with no separate copies.
 // suffixgpu_b200::vllm_prepare wraps sg_vllm_prepare, the per-step input
 // preparation of vLLM's GPU n-gram proposer, for the vLLM adapter.
 #include <ATen/ATen.h>
@@ -21,13 +25,35 @@
 
 namespace {
 
+// Address the kernel uses for `t`: its data pointer for a tensor on
+// `dev`, the mapped device address for a page-locked host tensor. Anything
+// else (pageable host memory, another device) is refused before a launch.
+int32_t* kernel_ptr(const at::Tensor& t, const at::Device& dev,
+                   const char* what) {
+  if (t.is_cuda()) {
+    TORCH_CHECK(t.device() == dev, what, " is on ", t.device(),
+                " but token_ids is on ", dev);
+    return t.data_ptr<int32_t>();
+  }
+  TORCH_CHECK(t.device().is_cpu(), what, " must be a CUDA tensor or a "
+              "page-locked host tensor");
+  void* d = nullptr;
+  TORCH_CHECK(t.numel() == 0 ||
+                  sg_mapped_host_ptr(t.data_ptr<int32_t>(), &d) == SG_OK,
+              what, " is a host tensor in pageable memory; pass a "
+              "page-locked one (tensor.pin_memory()) or a CUDA tensor");
+  return static_cast<int32_t*>(d);
+}
+
 std::vector<at::Tensor> local_draft(const at::Tensor& num_tokens,
                                     const at::Tensor& token_ids,
                                     const c10::optional<at::Tensor>& sampled,
                                     const c10::optional<at::Tensor>& valid_count,
                                     const c10::optional<at::Tensor>& mask,
                                     const at::Tensor& params, int64_t limit,
-                                    bool extras) {
+                                    bool extras,
+                                    const c10::optional<at::Tensor>& out_draft,
+                                    const c10::optional<at::Tensor>& out_num_valid) {
   TORCH_CHECK(token_ids.is_cuda() && num_tokens.is_cuda(),
               "suffixgpu_b200 ops need CUDA tensors");
   TORCH_CHECK(token_ids.scalar_type() == at::kInt && token_ids.dim() == 2 &&
@@ -59,18 +85,52 @@ std::vector<at::Tensor> local_draft(const at::Tensor& num_tokens,
   out.num_valid = base + b * k;
   std::vector<at::Tensor> res;
   res.reserve(7);
-  res.push_back(buf.narrow(0, 0, b * k).view({b, k}));
-  res.push_back(buf.narrow(0, b * k, b));
+  const at::Device dev = token_ids.device();
+  if (out_draft.has_value()) {
+    const at::Tensor& o = *out_draft;
+    TORCH_CHECK(o.scalar_type() == at::kInt && o.dim() == 2 &&
+                    o.size(0) == b && o.size(1) == k && o.is_contiguous(),
+                "out draft must be a contiguous int32 [B, k] tensor");
+    out.draft = kernel_ptr(o, dev, "out draft");
+    res.push_back(o);
+  } else {
+    res.push_back(buf.narrow(0, 0, b * k).view({b, k}));
+  }
+  if (out_num_valid.has_value()) {
+    const at::Tensor& o = *out_num_valid;
+    TORCH_CHECK(o.scalar_type() == at::kInt && o.dim() == 1 &&
+                    o.size(0) == b && o.is_contiguous(),
+                "out num_valid must be a contiguous int32 [B] tensor");
+    out.num_valid = kernel_ptr(o, dev, "out num_valid");
+    res.push_back(o);
+  } else {
+    res.push_back(buf.narrow(0, b * k, b));
+  }
   at::Tensor samp, vc, msk;
   if (sampled.has_value()) {
     samp = *sampled;
-    if (samp.scalar_type() != at::kInt || !samp.is_contiguous())
-      samp = samp.to(at::kInt).contiguous();
-    in.sampled = samp.data_ptr<int32_t>();
+    if (samp.is_cuda()) {
+      if (samp.scalar_type() != at::kInt || !samp.is_contiguous())
+        samp = samp.to(at::kInt).contiguous();
+    } else {
+      // a host tensor is read in place: no conversion into pageable memory
+      TORCH_CHECK(samp.scalar_type() == at::kInt && samp.is_contiguous(),
+                  "a host sampled tensor must be contiguous int32");
+    }
+    TORCH_CHECK(samp.dim() == 2 && samp.size(0) == b,
+                "sampled must be [B, T] with B = token_ids rows");
+    in.sampled = kernel_ptr(samp, dev, "sampled");
     in.sampled_cols = static_cast<int32_t>(samp.size(1));
     if (valid_count.has_value()) {
-      vc = valid_count->to(at::kInt).contiguous();
-      in.valid_count = vc.data_ptr<int32_t>();
+      vc = *valid_count;
+      if (vc.is_cuda()) {
+        vc = vc.to(at::kInt).contiguous();
+      } else {
+        TORCH_CHECK(vc.scalar_type() == at::kInt && vc.is_contiguous(),
+                    "a host valid_count tensor must be contiguous int32");
+      }
+      TORCH_CHECK(vc.numel() >= b, "valid_count has fewer than B entries");
+      in.valid_count = kernel_ptr(vc, dev, "valid_count");
     }
     out.new_counts = base + b * (k + 1);
     res.push_back(buf.narrow(0, b * (k + 1), b));
@@ -154,7 +214,8 @@ TORCH_LIBRARY(suffixgpu_b200, m) {
   m.def(
       "local_draft(Tensor num_tokens, Tensor token_ids, Tensor? sampled, "
       "Tensor? valid_count, Tensor? mask, Tensor params, int limit, "
-      "bool extras) -> Tensor[]");
+      "bool extras, Tensor? out_draft=None, Tensor? out_num_valid=None) "
+      "-> Tensor[]");
   m.def(
       "vllm_prepare(Tensor sampled, Tensor? discard, Tensor token_ids, "
       "Tensor num_tokens, int vocab_size) -> Tensor[]");

@@ -72,9 +72,13 @@ class LocalMatchKernel:
             sampled: torch.Tensor | None = None,
             valid_count: torch.Tensor | None = None,
             mask: torch.Tensor | None = None, limit: int | None = None,
-            extras: bool = False) -> dict:
+            extras: bool = False,
+            out: tuple[torch.Tensor, torch.Tensor] | None = None) -> dict:
         """One fused launch (the torch operator over sg_local_draft);
-        returns a dict of newly allocated output tensors."""
+        returns a dict of output tensors, newly allocated except the
+        (draft, num_valid) pair given as ``out``. ``sampled`` /
+        ``valid_count`` and ``out`` may be page-locked host tensors, which
+        the kernel reads and writes in place (no separate copies)."""
         if not (token_ids.is_cuda and num_tokens.is_cuda):
             require_cuda(num_tokens, token_ids)
         op = self._op
@@ -84,9 +88,13 @@ class LocalMatchKernel:
             # fills in the batch shape)
             self._params_t = torch.frombuffer(
                 bytearray(bytes(self.params(0, 1, 1))), dtype=torch.uint8)
-        res = op(num_tokens, token_ids, sampled, valid_count, mask,
-                 self._params_t,
-                 token_ids.shape[1] if limit is None else int(limit), extras)
+        lim = token_ids.shape[1] if limit is None else int(limit)
+        if out is None:
+            res = op(num_tokens, token_ids, sampled, valid_count, mask,
+                     self._params_t, lim, extras)
+        else:
+            res = op(num_tokens, token_ids, sampled, valid_count, mask,
+                     self._params_t, lim, extras, out[0], out[1])
         out = {"draft": res[0], "num_valid": res[1]}
         if sampled is not None:
             out["new_counts"] = res[2]

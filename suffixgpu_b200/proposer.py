@@ -110,18 +110,34 @@ class SuffixGPUDrafter:
         sampled_token_ids: torch.Tensor,
         valid_sampled_tokens_count: torch.Tensor | None = None,
         max_model_len: int | None = None,
+        *,
+        out: tuple[torch.Tensor, torch.Tensor] | None = None,
     ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         """update_state + eligibility mask + propose, all on device
         (proposer.py:186-214). Returns (draft [B,k] int32, num_valid [B]
-        int32, new_num_tokens [B] int32)."""
+        int32, new_num_tokens [B] int32).
+
+        Host buffers (no reference counterpart): ``sampled_token_ids`` and
+        ``valid_sampled_tokens_count`` may be page-locked host tensors, and
+        ``out=(draft, num_valid)`` names the tensors to fill, on the device
+        or page-locked on the host. The local step reads and writes those
+        host buffers from the kernel itself, so a host-driven loop makes
+        one launch per step and no copies; read them only after the stream
+        has passed the call (e.g. ``torch.cuda.current_stream()
+        .synchronize()``)."""
         s = token_ids_gpu.shape[1]
         limit = s if max_model_len is None else min(max_model_len, s)
         if self.global_index is None:
             o = self.local_kernel.run(
                 num_tokens_no_spec, token_ids_gpu,
                 sampled=sampled_token_ids,
-                valid_count=valid_sampled_tokens_count, limit=limit)
+                valid_count=valid_sampled_tokens_count, limit=limit,
+                out=out)
             return o["draft"], o["num_valid"], o["new_counts"]
+        # the global kernels read their inputs from device memory
+        sampled_token_ids = self._on_device(sampled_token_ids)
+        valid_sampled_tokens_count = self._on_device(
+            valid_sampled_tokens_count)
         # the global searches fork off before the local step (they read the
         # rows' tails as the local step's scatter will leave them)
         streams = self._aux_streams()
@@ -136,18 +152,19 @@ class SuffixGPUDrafter:
             extras=True)
         draft, nv = self.global_index.finish_global_step(pend, o, self,
                                                          streams)
-        return draft, nv, o["new_counts"]
+        return (*self._into(out, draft, nv), o["new_counts"])
 
     def propose(self, num_tokens_no_spec: torch.Tensor,
                 token_ids_gpu: torch.Tensor,
-                combined_mask: torch.Tensor | None = None
+                combined_mask: torch.Tensor | None = None, *,
+                out: tuple[torch.Tensor, torch.Tensor] | None = None
                 ) -> tuple[torch.Tensor, torch.Tensor]:
         """Draft from local history (and the global index when enabled)
         (proposer.py:216-327). Returns (draft [B,k] int32, num_valid [B]
-        int32)."""
+        int32); ``out`` as in propose_with_update."""
         if self.global_index is None:
             o = self.local_kernel.run(num_tokens_no_spec, token_ids_gpu,
-                                      mask=combined_mask)
+                                      mask=combined_mask, out=out)
             return o["draft"], o["num_valid"]
         streams = self._aux_streams()
         pend = self.global_index.start_global_step(
@@ -155,7 +172,23 @@ class SuffixGPUDrafter:
             streams=streams)
         o = self.local_kernel.run(num_tokens_no_spec, token_ids_gpu,
                                   mask=combined_mask, extras=True)
-        return self.global_index.finish_global_step(pend, o, self, streams)
+        return self._into(out, *self.global_index.finish_global_step(
+            pend, o, self, streams))
+
+    def _on_device(self, t: torch.Tensor | None) -> torch.Tensor | None:
+        if t is None or t.is_cuda:
+            return t
+        return t.to(self.device, non_blocking=True)
+
+    @staticmethod
+    def _into(out, draft: torch.Tensor, nv: torch.Tensor):
+        """Results into the caller's (draft, num_valid) tensors, if given
+        (asynchronous copies on the current stream)."""
+        if out is None:
+            return draft, nv
+        out[0].copy_(draft, non_blocking=True)
+        out[1].copy_(nv, non_blocking=True)
+        return out[0], out[1]
 
     def _aux_streams(self):
         """The two side streams of the global searches and the four events

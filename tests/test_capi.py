@@ -92,6 +92,11 @@ def test_invalid_arguments_rejected_without_gpu(libpath):
                                     2, 4, None, None, None, None) == 1
     assert L.sg_gather_tails_update(None, 8, 8, None, None, 0, None, 8, None,
                                     0, 4, None, None, None, None) == 0
+    # host-buffer address query: null arguments
+    dptr = ctypes.c_void_p(1)
+    assert L.sg_mapped_host_ptr(None, ctypes.byref(dptr)) == 1
+    buf = ctypes.create_string_buffer(64)
+    assert L.sg_mapped_host_ptr(ctypes.addressof(buf), None) == 1
 
 
 def test_torch_operator_registers():
@@ -102,5 +107,6 @@ def test_torch_operator_registers():
     schema = str(op.default._schema)
     assert schema.startswith("suffixgpu_b200::local_draft(Tensor num_tokens")
     assert "Tensor params" in schema and "-> Tensor[]" in schema
+    assert "Tensor? out_draft=None, Tensor? out_num_valid=None" in schema
     schema = str(_lib.torch_ops().vllm_prepare.default._schema)
     assert schema.startswith("suffixgpu_b200::vllm_prepare(Tensor sampled")
