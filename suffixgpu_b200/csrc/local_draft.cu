@@ -120,6 +120,23 @@ __device__ __forceinline__ int warp_candidates(const int* ge, int P, int C,
   return (lane > 0 && prev == cand) ? 0 : cand;
 }
 
+// update_state's writes for one row (proposer.py:166-188), by one warp:
+// row[base + j] = sampled[j] for j < cnt with sampled[j] != -1 and the
+// position inside the row; the new count goes to *new_count.
+__device__ __forceinline__ void scatter_to_row(int32_t* row, int lane, int T,
+                                               const int32_t* srow,
+                                               int my_samp, long long base,
+                                               long long cnt, int S,
+                                               long long q,
+                                               int32_t* new_count) {
+  for (int j = lane; j < T; j += 32) {
+    const int val = j < 32 ? my_samp : srow[j];
+    const long long pos = base + j;
+    if (j < cnt && val != -1 && pos < S && pos >= 0) row[pos] = val;
+  }
+  if (lane == 0) *new_count = static_cast<int32_t>(q);
+}
+
 template <int RJ, int NC>
 __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
     local_draft_kernel(const LocalArgs a) {
@@ -163,11 +180,41 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
   // ---- 1. row bookkeeping (warp 0) + bulk load ----------------------------
   int my_samp = -1;  // warp 0, lane j < T: sampled[b, j]
   if (warp == 0) {
+    // the ids may live in host memory: their load goes out first and the
+    // bulk copy does not wait for it (below)
+    if (srow && lane < T) my_samp = srow[lane];
     const long long base = a.in.num_tokens[b];
+    // Tokens to bulk-copy (whole 16-byte words; a last partial word is
+    // copied whole when it lies inside the row's S tokens, and positions
+    // past the count are never read as tokens). Without valid counts the
+    // update adds at most T ids, so base + T tokens cover the row and the
+    // copy starts before the ids arrive; if the row turns out not to
+    // draft, the copy is waited for and unused. A remaining ragged tail,
+    // or a row that is not 16-byte aligned, is read with plain loads after
+    // the barrier, while the bulk copy is in flight.
+    auto start_copy = [&](long long upto) -> int {
+      const int n = static_cast<int>(upto < 0 ? 0 : (upto < S ? upto : S));
+      int nal = n & ~3;
+      if (nal < n && nal + 4 <= S) nal += 4;
+      if ((reinterpret_cast<uintptr_t>(row) & 15) != 0) nal = 0;
+      if (lane == 0 && nal > 0) {
+        mbar_init(bar, 1);
+        const uint32_t bytes = static_cast<uint32_t>(nal) * 4u;
+        mbar_arrive_expect_tx(bar, bytes);
+        constexpr uint32_t kChunk = 32768;
+        for (uint32_t off = 0; off < bytes; off += kChunk) {
+          const uint32_t nb = bytes - off < kChunk ? bytes - off : kChunk;
+          bulk_g2s(reinterpret_cast<unsigned char*>(tok_s) + off,
+                   reinterpret_cast<const unsigned char*>(row) + off, nb, bar);
+        }
+      }
+      return nal;
+    };
+    const bool early = !(srow && a.in.valid_count);
+    int nal = early ? start_copy(srow ? base + T : base) : 0;
     long long cnt = 0, q = base;
     int m;
     if (srow) {
-      if (lane < T) my_samp = srow[lane];
       if (a.in.valid_count) {
         cnt = a.in.valid_count[b];
       } else {
@@ -183,30 +230,23 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
     }
     const long long nl = q < 0 ? 0 : (q < S ? q : S);
     const int nload = m ? static_cast<int>(nl) : 0;
-    int nal = nload & ~3;
-    if ((reinterpret_cast<uintptr_t>(row) & 15) != 0) nal = 0;
-    // a ragged tail of up to 32 tokens is read here, beside the bulk copy
-    // (disjoint shared-memory ranges)
-    if (nload - nal <= 32 && nal + lane < nload) tok_s[nal + lane] = row[nal + lane];
+    if (!early) nal = start_copy(nload);
     if (lane == 0) {
-      if (srow) a.out.new_counts[b] = static_cast<int32_t>(q);
       s_q = q; s_base = base; s_cnt = cnt; s_mask = m;
       s_nload = nload; s_nal = nal;
-      if (nal > 0) {
-        mbar_init(bar, 1);
-        const uint32_t bytes = static_cast<uint32_t>(nal) * 4u;
-        mbar_arrive_expect_tx(bar, bytes);
-        constexpr uint32_t kChunk = 32768;
-        for (uint32_t off = 0; off < bytes; off += kChunk) {
-          const uint32_t n = bytes - off < kChunk ? bytes - off : kChunk;
-          bulk_g2s(reinterpret_cast<unsigned char*>(tok_s) + off,
-                   reinterpret_cast<const unsigned char*>(row) + off, n, bar);
-        }
-      }
     }
   } else {
-    // other warps: empty their vote tables while the loads are in flight
+    // other warps: empty the vote tables (warp 1 also warp 0's) and the
+    // per-warp histograms while the loads are in flight
     vote_table_clear(vs);
+    if (warp == 1) {
+      VoteScratch v0 = vs;
+      const ptrdiff_t back = static_cast<ptrdiff_t>(L.warp_bytes / 4);
+      v0.act -= back;
+      v0.hkey -= back;
+      v0.hcnt -= back;
+      vote_table_clear(v0);
+    }
     for (int i = t - 32; i < (P + 2) * kLocalWarps; i += kLocalThreads - 32)
       whist[i] = 0;
   }
@@ -215,9 +255,9 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
   // q clamped into int range: positions are < S < 2^23
   const int q32 = q > INT32_MAX ? INT32_MAX : (q < INT32_MIN ? INT32_MIN : static_cast<int>(q));
   const int mask = s_mask, nload = s_nload, nal = s_nal;
-  // the whole row when it is not 16-byte aligned
-  if (nload - nal > 32)
-    for (int i = nal + t; i < nload; i += kLocalThreads) tok_s[i] = row[i];
+  // the ragged tail, or the whole row when it is not 16-byte aligned
+  // (disjoint from the bulk copy's shared-memory range)
+  for (int i = nal + t; i < nload; i += kLocalThreads) tok_s[i] = row[i];
   bool timed_out = false;
   if (nal > 0 && !mbar_wait(bar, 0)) {
     // A bulk copy of resident memory always lands; should the bound ever
@@ -228,38 +268,36 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
   if (__syncthreads_or(timed_out)) {
     for (int d = t; d < K; d += kLocalThreads)
       a.out.draft[static_cast<long long>(b) * K + d] = -1;
-    if (t == 0) a.out.num_valid[b] = -1;
+    if (t == 0) {
+      a.out.num_valid[b] = -1;
+      if (srow) a.out.new_counts[b] = static_cast<int32_t>(q);
+    }
     return;
   }
-  if (warp == 0) {
-    if (lane == 0 && nal > 0) mbar_inval(bar);
-    // scatter-append the sampled ids (update_state, proposer.py:166-188);
-    // all loads have landed, so the HBM writes cannot race them
+  if (warp == 0 && mask) {
+    // scatter-append the sampled ids into the shared copy (update_state,
+    // proposer.py:166-188); the HBM row gets them once the match scan has
+    // started (no global store ahead of the next barrier)
     if (srow) {
       const long long base = s_base, cnt = s_cnt;
       for (int j = lane; j < T; j += 32) {
         const int val = j < 32 ? my_samp : srow[j];
         const long long pos = base + j;
-        if (j < cnt && val != -1 && pos < S && pos >= 0) {
-          row[pos] = val;
-          if (pos < nload) tok_s[pos] = val;
-        }
+        if (j < cnt && val != -1 && pos < nload && pos >= 0) tok_s[pos] = val;
       }
     }
     __syncwarp();  // this warp's scatter into tok_s is visible below
-    if (mask) {
-      // pattern, newest-first: pat[t] = tok[q-1-t] or -2 before the start
-      // (local_matcher.py:103-112); reads clamp to the buffer like gather
-      for (int i = lane; i < P; i += 32) {
-        const long long x = q - 1 - i;
-        pat[i] = x < 0 ? -2 : tok_s[x < S ? x : S - 1];
-      }
+    // pattern, newest-first: pat[t] = tok[q-1-t] or -2 before the start
+    // (local_matcher.py:103-112); reads clamp to the buffer like gather
+    for (int i = lane; i < P; i += 32) {
+      const long long x = q - 1 - i;
+      pat[i] = x < 0 ? -2 : tok_s[x < S ? x : S - 1];
     }
-    __syncwarp();
-    vote_table_clear(vs);
   }
   __syncthreads();
 
+  // the update's HBM writes: all loads of the row have landed (a drafting
+  // row issues them once its match scan has started)
   if (!mask) {
     for (int d = t; d < K; d += kLocalThreads)
       a.out.draft[static_cast<long long>(b) * K + d] = -1;
@@ -270,8 +308,14 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
       if (a.out.best_occ) a.out.best_occ[b] = 0;
       if (a.out.row_mask) a.out.row_mask[b] = 0;
     }
+    if (warp == 0 && srow)
+      scatter_to_row(row, lane, T, srow, my_samp, s_base, s_cnt, S, q,
+                     a.out.new_counts + b);
     return;
   }
+  if (warp == 0 && srow)
+    scatter_to_row(row, lane, T, srow, my_samp, s_base, s_cnt, S, q,
+                   a.out.new_counts + b);
 
   // ---- 2. match_back: ordered hit lists per warp segment -----------------
   // Each warp owns a contiguous segment of 1024-token chunks. In a chunk,
@@ -340,7 +384,7 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
     const int pt1 = P > 1 ? pat[1] : INT32_MIN;
     const int pt2 = P > 2 ? pat[2] : INT32_MIN;
     const int pt3 = P > 3 ? pat[3] : INT32_MIN;
-    int h1 = 0, h2 = 0, h3 = 0, h4 = 0;
+    int h1 = 0, h2 = 0, h3 = 0, h4 = 0, hp = 0;
     for (int i = lane; i < nh; i += 32) {
       const int e = my_hits[i];
       const int t1 = e >= 2 ? tok_s[e - 2] : -1;
@@ -367,13 +411,15 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
       h2 += m == 2;
       h3 += m == 3;
       h4 += m == 4;
-      if (m > 4) atomicAdd(&my_ge[m], 1);
+      hp += m == P && P > 4;  // full-length matches: no atomic per hit
+      if (m > 4 && m < P) atomicAdd(&my_ge[m], 1);
       my_hits[i] = (e << 8) | m;
     }
     h1 = warp_sum(h1);
     h2 = warp_sum(h2);
     h3 = warp_sum(h3);
     h4 = warp_sum(h4);
+    hp = warp_sum(hp);
     __syncwarp();  // this warp's atomics on my_ge have landed
     // histogram -> #{hits with mb >= L}, suffix sums from the top chunk
     int above = 0;  // #{hits with mb above this chunk of lengths}
@@ -381,6 +427,7 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
       const int Lx = L0 + lane;
       int v = Lx <= P ? my_ge[Lx] : 0;
       v += Lx == 1 ? h1 : Lx == 2 ? h2 : Lx == 3 ? h3 : Lx == 4 ? h4 : 0;
+      if (Lx == P && P > 4) v += hp;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int u = __shfl_down_sync(SG_FULL_MASK, v, o);
