@@ -161,6 +161,13 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
   __shared__ long long s_q, s_base, s_cnt;
   __shared__ int s_mask, s_nload, s_nal;
 
+  // Programmatic dependent launch: the next kernel on the stream may be
+  // scheduled as soon as every CTA of this one has started, and this one
+  // waits here until the kernel before it has completed and its writes are
+  // visible (both are no-ops for an ordinary launch). Every global access
+  // below comes after the wait.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int b = blockIdx.x;
   const int t = threadIdx.x;
   const int lane = lane_id(), warp = warp_id();
@@ -589,7 +596,24 @@ static int launch_local_nc(const LocalArgs& a, size_t smem, cudaStream_t st) {
   static int cache[64] = {0};
   const int rc = ensure_dyn_smem(local_draft_kernel<RJ, NC>, smem, cache);
   if (rc != SG_OK) return rc;
-  local_draft_kernel<RJ, NC><<<a.p.batch, kLocalThreads, smem, st>>>(a);
+  // launched with programmatic stream serialization: the kernel's CTAs
+  // can be resident while the previous kernel on the stream finishes
+  // (griddepcontrol in the kernel keeps the data dependency)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.p.batch));
+  cfg.blockDim = dim3(kLocalThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, local_draft_kernel<RJ, NC>, a);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return SG_ERR_CUDA;
+  }
   return check_launch();
 }
 
