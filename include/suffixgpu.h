@@ -85,6 +85,13 @@ typedef struct sg_local_inputs {
   const int32_t* sampled;    /* [B, sampled_cols] ids, -1 padded; NULL =
                                 propose mode (no update) */
   int32_t sampled_cols;      /* T */
+  int32_t host_ids;          /* 0, or nonzero when sampled (and valid_count)
+                                are page-locked host memory that the CPU
+                                wrote before the call: the kernel then reads
+                                them before waiting for the previous kernel
+                                on the stream, hiding the host-link latency.
+                                Must stay 0 if GPU work still in flight
+                                writes them. */
   const int32_t* valid_count; /* [B] or NULL: #(sampled[b, :] != -1) */
   const uint8_t* mask;       /* propose mode: [B] rows allowed to draft, or
                                 NULL = all rows */

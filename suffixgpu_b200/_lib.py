@@ -43,6 +43,7 @@ class LocalInputs(Structure):
         ("token_ids", c_void_p),
         ("sampled", c_void_p),
         ("sampled_cols", c_int32),
+        ("host_ids", c_int32),
         ("valid_count", c_void_p),
         ("mask", c_void_p),
         ("limit", c_int64),

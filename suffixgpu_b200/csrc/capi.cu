@@ -45,7 +45,7 @@ extern "C" const char* sg_status_string(int status) {
 
 extern "C" int sg_last_cuda_error(void) { return sg::g_last_cuda_error; }
 
-extern "C" int sg_abi_version(void) { return (1 << 16) | 1; }
+extern "C" int sg_abi_version(void) { return (1 << 16) | 2; }
 
 extern "C" int sg_mapped_host_ptr(const void* host_ptr, void** device_ptr) {
   if (!host_ptr || !device_ptr) return SG_ERR_INVALID;

@@ -161,15 +161,25 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
   __shared__ long long s_q, s_base, s_cnt;
   __shared__ int s_mask, s_nload, s_nal;
 
-  // Programmatic dependent launch: the next kernel on the stream may be
-  // scheduled as soon as every CTA of this one has started, and this one
-  // waits here until the kernel before it has completed and its writes are
-  // visible (both are no-ops for an ordinary launch). Every global access
-  // below comes after the wait.
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int b = blockIdx.x;
   const int t = threadIdx.x;
+  // Programmatic dependent launch: the next kernel on the stream may be
+  // scheduled as soon as every CTA of this one has started, and this one
+  // waits until the kernel before it has completed and its writes are
+  // visible (both are no-ops for an ordinary launch). Every global access
+  // comes after the wait, except the sampled ids / valid counts the CPU
+  // wrote to page-locked host memory (host_ids): their host-link round
+  // trip overlaps the wait.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  int my_samp = -1;  // warp 0, lane j < T: sampled[b, j]
+  int host_vc = 0;   // warp 0: valid_count[b] read early
+  if (a.in.host_ids && threadIdx.x < 32 && a.in.sampled) {
+    const int T0 = a.in.sampled_cols;
+    if (static_cast<int>(threadIdx.x) < T0)
+      my_samp = a.in.sampled[static_cast<long long>(b) * T0 + threadIdx.x];
+    if (a.in.valid_count) host_vc = a.in.valid_count[b];
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane = lane_id(), warp = warp_id();
   const unsigned lt_mask = (1u << lane) - 1u;
   int32_t* row = a.in.token_ids + static_cast<long long>(b) * p.row_stride;
@@ -185,11 +195,10 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
   vs.hshift = 33 - __ffs(L.H);
 
   // ---- 1. row bookkeeping (warp 0) + bulk load ----------------------------
-  int my_samp = -1;  // warp 0, lane j < T: sampled[b, j]
   if (warp == 0) {
     // the ids may live in host memory: their load goes out first and the
     // bulk copy does not wait for it (below)
-    if (srow && lane < T) my_samp = srow[lane];
+    if (srow && lane < T && !a.in.host_ids) my_samp = srow[lane];
     const long long base = a.in.num_tokens[b];
     // Tokens to bulk-copy (whole 16-byte words; a last partial word is
     // copied whole when it lies inside the row's S tokens, and positions
@@ -223,7 +232,7 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
     int m;
     if (srow) {
       if (a.in.valid_count) {
-        cnt = a.in.valid_count[b];
+        cnt = a.in.host_ids ? host_vc : a.in.valid_count[b];
       } else {
         cnt = __popc(__ballot_sync(SG_FULL_MASK, lane < T && my_samp != -1));
         for (int j0 = 32; j0 < T; j0 += 32)  // T > 32 (rare)

@@ -10,7 +10,8 @@
 // The sampled ids (and valid counts) may be page-locked host tensors and
 // the draft / num_valid outputs may be caller-provided tensors, on the
 // device or in page-locked host memory: the kernel then reads and writes
-// those host buffers directly, with no separate copies.
+// those host buffers directly, with no separate copies. Host inputs are
+// taken to be written by the CPU (not by GPU work still in flight).
 // suffixgpu_b200::vllm_prepare wraps sg_vllm_prepare, the per-step input
 // preparation of vLLM's GPU n-gram proposer, for the vLLM adapter.
 #include <ATen/ATen.h>
@@ -132,6 +133,9 @@ std::vector<at::Tensor> local_draft(const at::Tensor& num_tokens,
       TORCH_CHECK(vc.numel() >= b, "valid_count has fewer than B entries");
       in.valid_count = kernel_ptr(vc, dev, "valid_count");
     }
+    // page-locked host inputs are the CPU's writes: the kernel may read
+    // them before the previous kernel on the stream has finished
+    in.host_ids = !samp.is_cuda() && (!vc.defined() || !vc.is_cuda());
     out.new_counts = base + b * (k + 1);
     res.push_back(buf.narrow(0, b * (k + 1), b));
   } else {

@@ -124,7 +124,10 @@ class SuffixGPUDrafter:
         host buffers from the kernel itself, so a host-driven loop makes
         one launch per step and no copies; read them only after the stream
         has passed the call (e.g. ``torch.cuda.current_stream()
-        .synchronize()``)."""
+        .synchronize()``). Host inputs must hold the CPU's writes: the
+        kernel may read them before the previous kernel on the stream has
+        finished, so they must not be the target of GPU work still in
+        flight (a non-blocking device-to-host copy, say)."""
         s = token_ids_gpu.shape[1]
         limit = s if max_model_len is None else min(max_model_len, s)
         if self.global_index is None:

@@ -54,6 +54,7 @@ def test_ctypes_struct_layout_matches_header():
     assert DraftParams.vote_alpha.offset == 52
     assert ctypes.sizeof(LocalInputs) == 56
     assert LocalInputs.limit.offset == 48
+    assert LocalInputs.host_ids.offset == 28
     assert ctypes.sizeof(LocalOutputs) == 56
 
 
