@@ -56,7 +56,9 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=400)
     ap.add_argument("--cpu-rows", type=int, default=256,
                     help="rows per step in the CPU sample")
-    ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--cpu-steps", type=int, default=10,
+                    help="timed decode steps of the CPU sample (about "
+                         "10-30 s of CPU work over all workers)")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the end-to-end API leg (profiling runs)")
     ap.add_argument("--no-cpu", action="store_true",
@@ -928,18 +930,20 @@ def _traffic():
 # CPU baseline (oracle port of the reference's torch CPU path)
 # ---------------------------------------------------------------------------
 def _cpu_chunk(payload):
-    rows, steps, cfg = payload
+    rows, steps, warm, cfg = payload
     sys.path.insert(0, ROOT)
     from oracle import suffix_oracle as so
     tok, q, samp = rows
     d = so.SuffixDrafter(**cfg)
+    for j in range(warm):  # untimed decode steps
+        _, _, q = d.propose_with_update(q, tok, samp[j])
     t0 = time.perf_counter()
-    for j in range(steps):
+    for j in range(warm, warm + steps):
         _, _, q = d.propose_with_update(q, tok, samp[j])
     return time.perf_counter() - t0
 
 
-def cpu_baseline(args, data, cores=None) -> dict:
+def cpu_baseline(args, data, cores=None, warm: int = 1) -> dict:
     """Reference algorithm (numpy port) on a bounded sample: cpu_rows rows
     of config 2 for cpu_steps decode steps, rows split across one process
     per host core (rows are independent). Each worker times its own
@@ -949,14 +953,15 @@ def cpu_baseline(args, data, cores=None) -> dict:
     cores = cores or max(1, os.cpu_count() or 1)
     rows = min(args.cpu_rows, B)
     steps = args.cpu_steps
+    warm = max(0, min(warm, data["sampled"].shape[0] - steps))
     tok = data["token_ids"][:rows].copy()
     q = data["num_tokens"][:rows].copy()
-    samp = data["sampled"][:steps, :rows].copy()
+    samp = data["sampled"][:warm + steps, :rows].copy()
     nproc = min(cores, rows)
     bounds = np.linspace(0, rows, nproc + 1).astype(int)
     from suffixgpu_b200.workloads import CONFIG2_DRAFTER
     chunks = [((tok[a:b_].copy(), q[a:b_].copy(), samp[:, a:b_].copy()),
-               steps, dict(CONFIG2_DRAFTER))
+               steps, warm, dict(CONFIG2_DRAFTER))
               for a, b_ in zip(bounds[:-1], bounds[1:]) if b_ > a]
     t0 = time.perf_counter()
     with ProcessPoolExecutor(max_workers=len(chunks),
@@ -966,7 +971,8 @@ def cpu_baseline(args, data, cores=None) -> dict:
     slowest = max(times)
     return {"value": rows * steps / slowest, "unit": "rows/s",
             "cores": len(chunks), "kind": "port",
-            "sample": f"{rows} rows of config 2 x {steps} decode steps, "
+            "sample": f"{rows} rows of config 2 x {steps} timed decode "
+                      f"steps after {warm} untimed, "
                       f"numpy restatement of the reference CPU path, "
                       f"{len(chunks)} worker processes; slowest worker "
                       f"{slowest:.2f} s compute, {wall:.2f} s wall with "
@@ -978,11 +984,12 @@ def run_reference(args):
     if rank != 0:
         return None
     data = workload(0)
-    cb = cpu_baseline(args, data)
+    warm = max(1, min(args.warmup, 5))
+    cb = cpu_baseline(args, data, warm=warm)
     v = cb["value"]
     return {
         "metric": METRIC, "value": v, "unit": "rows/s", "n_gpus": 0,
-        "steps": args.cpu_steps, "warmup": 0,
+        "steps": args.cpu_steps, "warmup": warm,
         "ms_per_step": 1e3 * min(args.cpu_rows, B) / v,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int32",
