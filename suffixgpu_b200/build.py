@@ -82,6 +82,20 @@ def build(verbose: bool = False, extra_flags: list[str] | None = None) -> str:
     return LIB
 
 
+def _loaded_cxx_runtime() -> str | None:
+    """Path of the C++ runtime (libstdc++) this process has loaded -- the
+    one torch uses, which the operator library must share."""
+    try:
+        with open("/proc/self/maps") as f:
+            for line in f:
+                path = line.split()[-1]
+                if os.path.basename(path).startswith("libstdc++.so"):
+                    return path
+    except OSError:
+        pass
+    return None
+
+
 def build_torch_ops(verbose: bool = False) -> str:
     """Compile the torch operator (incrementally) against torch's headers
     and libraries, linked to the kernel library (found next to it)."""
@@ -98,6 +112,13 @@ def build_torch_ops(verbose: bool = False) -> str:
     cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared",
            f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
            src, "-o", TORCH_LIB, "-I" + cuda_inc]
+    # Link against the process's own libstdc++ by path: a compiler whose
+    # shared libstdc++ link is missing would otherwise fall back to the
+    # static archive, and a second C++ runtime inside this library crashes
+    # as soon as it formats a number into an error message.
+    rt = _loaded_cxx_runtime()
+    if rt:
+        cmd.append(rt)
     cmd += ["-I" + p for p in ce.include_paths(device_type="cuda")]
     cmd += ["-L" + p for p in ce.library_paths(device_type="cuda")]
     cmd += ["-L" + PKG, "-lsuffixgpu_b200", "-Wl,-rpath,$ORIGIN",

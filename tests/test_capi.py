@@ -111,3 +111,21 @@ def test_torch_operator_registers():
     assert "Tensor? out_draft=None, Tensor? out_num_valid=None" in schema
     schema = str(_lib.torch_ops().vllm_prepare.default._schema)
     assert schema.startswith("suffixgpu_b200::vllm_prepare(Tensor sampled")
+
+
+def test_torch_operator_shares_the_process_cxx_runtime():
+    """The operator library must use the process's shared libstdc++, not
+    a static copy: a second C++ runtime inside it crashed the process when
+    an error message formatted a number."""
+    import shutil
+    import subprocess
+    from suffixgpu_b200 import _lib, build
+    _lib.torch_ops()
+    nm = shutil.which("nm")
+    if nm is None:
+        pytest.skip("nm is not installed")
+    out = subprocess.run([nm, "-D", "--defined-only", build.TORCH_LIB],
+                         capture_output=True, text=True, check=True).stdout
+    # libstdc++ internals that only a statically linked runtime exports
+    assert "_txnal_cow_string_D1" not in out
+    assert "__codecvt_utf8_base" not in out

@@ -138,3 +138,19 @@ def test_global_drafter_host_buffers_equal_device_call():
         torch.cuda.synchronize(DEV)
         assert torch.equal(hd, dd.cpu()) and torch.equal(hnv, nvd.cpu())
         assert torch.equal(n[0], n[1])
+
+
+def test_rejected_settings_raise_instead_of_crashing():
+    """Settings the kernel cannot run (draft length above 64; a row layout
+    beyond shared memory) raise RuntimeError with the library's status."""
+    tok = torch.zeros(4, 97, dtype=torch.int32, device=DEV)
+    n = torch.full((4,), 50, dtype=torch.int32, device=DEV)
+    samp = torch.ones(4, 3, dtype=torch.int32, device=DEV)
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        SuffixGPUDrafter(device=DEV, k=65).propose_with_update(n, tok, samp)
+    big = torch.zeros(4, 30000, dtype=torch.int32, device=DEV)
+    d = SuffixGPUDrafter(device=DEV, k=12, max_pattern_len=20,
+                         max_occurrences=1024, num_backoff=10)
+    with pytest.raises(RuntimeError, match="beyond supported limits"):
+        d.propose_with_update(n, big, samp)
+    torch.cuda.synchronize(DEV)
