@@ -7,10 +7,12 @@
 // [B,S], the occurrence lists and the [B,C,R,K] continuation block in HBM;
 // here a single kernel keeps everything for a row in shared memory:
 //
-//   1. Warp 0 reads the row's count and sampled ids; one thread issues a
-//      TMA bulk copy (cp.async.bulk + mbarrier) of the committed tokens into
-//      shared memory; the sampled ids are then scattered into both the
-//      shared copy and the HBM buffer (update_state semantics).
+//   1. Warp 0 reads the row's count and sampled ids; as soon as the count
+//      is in, one thread issues a TMA bulk copy (cp.async.bulk + mbarrier)
+//      of the tokens the update can leave committed (count + T) into
+//      shared memory. The sampled ids are scattered into the shared copy,
+//      and into the HBM buffer once the match scan has started
+//      (update_state semantics).
 //   2. match_back for every end position i < q. Each warp owns a contiguous
 //      segment of positions and appends the nonzero ones, in position order,
 //      to its own hit list (one packed prefix sum per 256 words, no
