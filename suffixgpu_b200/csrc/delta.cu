@@ -465,6 +465,7 @@ extern "C" int sg_delta_match_backoff(
     int32_t num_caps, int32_t max_occ, const uint8_t* row_mask,
     int64_t* out_len, int64_t* out_pos, int64_t* out_cnt,
     sg_stream_t stream) {
+  sg::NvtxScope nvtx_range("sg_delta_match_backoff");
   if (delta_capacity < 1 || batch < 0 || query_width < 1 || max_len < 1 ||
       num_caps < 1 || num_caps > kDMaxCaps || max_occ < 1)
     return SG_ERR_INVALID;

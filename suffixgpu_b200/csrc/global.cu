@@ -499,6 +499,7 @@ extern "C" int sg_gather_tails_update(
     const int32_t* valid_count, int64_t limit, const uint8_t* mask,
     int32_t batch, int32_t pattern_len, int32_t* tails, int64_t* tail_len,
     uint8_t* row_mask, sg_stream_t stream) {
+  sg::NvtxScope nvtx_range("sg_gather_tails_update");
   if (batch < 0 || seq_len < 1 || row_stride < seq_len || pattern_len < 1 ||
       (sampled && sampled_cols < 1))
     return SG_ERR_INVALID;
@@ -522,6 +523,7 @@ extern "C" int sg_global_candidates(
     int32_t has_spec_factor, float spec_factor, float spec_offset,
     int64_t* match_len, int32_t* cont, int64_t* occ_count, int64_t* spec_cap,
     sg_stream_t stream) {
+  sg::NvtxScope nvtx_range("sg_global_candidates");
   if (batch < 0 || num_caps < 1 || num_caps > kGMaxCaps || max_occ < 1 ||
       k < 1 || capacity < 1 || delta_capacity < 1)
     return SG_ERR_INVALID;
@@ -567,6 +569,7 @@ extern "C" int sg_global_draft(
     float min_token_prob, float alpha, const float* local_score,
     const uint8_t* row_mask, int32_t* draft, int32_t* num_valid,
     sg_stream_t stream) {
+  sg::NvtxScope nvtx_range("sg_global_draft");
   if (batch < 0 || num_caps < 1 || num_caps > kGMaxCaps || max_occ < 1 ||
       max_occ > 1024 || k < 1 || k > 64 || capacity < 1 ||
       delta_capacity < 1)

@@ -642,6 +642,7 @@ extern "C" int sg_local_draft(const sg_draft_params* params,
                               const sg_local_inputs* in,
                               const sg_local_outputs* out,
                               sg_stream_t stream) {
+  sg::NvtxScope nvtx_range("sg_local_draft");
   if (!params || !in || !out) return SG_ERR_INVALID;
   const sg_draft_params& p = *params;
   if (p.batch < 0 || p.seq_len < 1 || p.row_stride < p.seq_len || p.k < 1 ||

@@ -253,6 +253,7 @@ extern "C" int sg_expand_chain(const int32_t* cont, int32_t rows,
                                int32_t* chain, int64_t* num_valid,
                                int64_t* num_emit, float* score,
                                sg_stream_t stream) {
+  sg::NvtxScope nvtx_range("sg_expand_chain");
   if (rows < 0 || max_occ < 1 || max_occ > 1024 || k < 1) return SG_ERR_INVALID;
   if (rows == 0) return SG_OK;
   if (!cont || !num_occ || !chain || !num_valid || !num_emit || !score)

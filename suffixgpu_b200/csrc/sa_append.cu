@@ -358,6 +358,7 @@ extern "C" int sg_suffix_array_append(
     int64_t evicted, int64_t kept_len, int32_t prev_rounds, int32_t* sa_out,
     void* workspace, size_t ws_bytes, int32_t* rounds_out,
     sg_stream_t stream) {
+  sg::NvtxScope nvtx_range("sg_suffix_array_append");
   if (n < 0 || prev_n < 0 || evicted < 0 || kept_len < 0 || prev_rounds < 0)
     return SG_ERR_INVALID;
   if (n >= (int64_t(1) << 31) - 1 || prev_n >= (int64_t(1) << 31) - 1)

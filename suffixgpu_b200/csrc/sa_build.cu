@@ -987,6 +987,7 @@ extern "C" int sg_build_suffix_array(const int32_t* tokens, int64_t n,
                                      int32_t* sa_out, void* workspace,
                                      size_t ws_bytes, int32_t* rounds_out,
                                      sg_stream_t stream) {
+  sg::NvtxScope nvtx_range("sg_build_suffix_array");
   if (n < 0) return SG_ERR_INVALID;
   if (n >= (int64_t(1) << 31) - 1) return SG_ERR_UNSUPPORTED;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

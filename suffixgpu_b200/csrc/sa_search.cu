@@ -442,6 +442,7 @@ extern "C" int sg_sa_search(const int32_t* sa, const int32_t* corpus,
                             int32_t width, const int64_t* pattern_len,
                             int64_t* out_start, int64_t* out_end,
                             sg_stream_t stream) {
+  sg::NvtxScope nvtx_range("sg_sa_search");
   if (n < 1 || batch < 0 || width < 1) return SG_ERR_INVALID;
   if (batch == 0) return SG_OK;
   if (!sa || !corpus || !pattern || !pattern_len || !out_start || !out_end)
@@ -475,6 +476,7 @@ extern "C" int sg_suffix_match_backoff(
     int32_t max_len, const int64_t* caps, int32_t num_caps,
     const uint8_t* row_mask, int64_t* out_len, int64_t* out_start,
     int64_t* out_end, sg_stream_t stream) {
+  sg::NvtxScope nvtx_range("sg_suffix_match_backoff");
   if (n < 1 || batch < 0 || query_width < 1 || max_len < 1 || num_caps < 1)
     return SG_ERR_INVALID;
   if (batch == 0) return SG_OK;

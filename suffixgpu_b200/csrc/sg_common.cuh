@@ -8,7 +8,19 @@
 
 #define SG_FULL_MASK 0xffffffffu
 
+#include <nvtx3/nvToolsExt.h>
+
 namespace sg {
+
+// Host-side NVTX range around an entry point: named ranges for nsys / ncu
+// (--nvtx) timelines; without an attached tool a push / pop costs a few
+// nanoseconds.
+struct NvtxScope {
+  explicit NvtxScope(const char* name) { nvtxRangePushA(name); }
+  ~NvtxScope() { nvtxRangePop(); }
+  NvtxScope(const NvtxScope&) = delete;
+  NvtxScope& operator=(const NvtxScope&) = delete;
+};
 
 // Host-side: remember the last CUDA error seen by an entry point.
 void set_cuda_error(cudaError_t e);
