@@ -19,12 +19,34 @@
 #include <c10/cuda/CUDAStream.h>
 #include <torch/library.h>
 
+#include <cuda_runtime_api.h>
+
 #include <cstring>
+#include <string>
 #include <vector>
 
 #include "../../include/suffixgpu.h"
 
 namespace {
+
+template <typename T>
+T* ptr_or_null(const c10::optional<at::Tensor>& t) {
+  return t.has_value() ? t->data_ptr<T>() : nullptr;
+}
+
+void check_status(const char* what, int st) {
+  // numbers are formatted here, into a std::string, before TORCH_CHECK
+  TORCH_CHECK(st == SG_OK, std::string(what) + " failed: " +
+                               sg_status_string(st) + " (status " +
+                               std::to_string(st) + ", cuda error " +
+                               std::to_string(sg_last_cuda_error()) + ")");
+}
+
+void check_cuda(cudaError_t e) {
+  TORCH_CHECK(e == cudaSuccess, std::string("CUDA error in the global step: ") +
+                                    cudaGetErrorString(e));
+}
+
 
 // Address the kernel uses for `t`: its data pointer for a tensor on
 // `dev`, the mapped device address for a page-locked host tensor. Anything
@@ -161,8 +183,7 @@ std::vector<at::Tensor> local_draft(const at::Tensor& num_tokens,
       &p, &in, &out,
       reinterpret_cast<sg_stream_t>(
           c10::cuda::getCurrentCUDAStream(token_ids.device().index()).stream()));
-  TORCH_CHECK(st == SG_OK, "sg_local_draft failed: ", sg_status_string(st),
-              " (status ", st, ", cuda error ", sg_last_cuda_error(), ")");
+  check_status("sg_local_draft", st);
   return res;
 }
 
@@ -206,10 +227,126 @@ std::vector<at::Tensor> vllm_prepare(const at::Tensor& sampled,
       vocab_size, base, base + b, base + 2 * b,
       reinterpret_cast<sg_stream_t>(
           c10::cuda::getCurrentCUDAStream(token_ids.device().index()).stream()));
-  TORCH_CHECK(st == SG_OK, "sg_vllm_prepare failed: ", sg_status_string(st),
-              " (status ", st, ", cuda error ", sg_last_cuda_error(), ")");
+  check_status("sg_vllm_prepare", st);
   return {buf.narrow(0, 0, b), buf.narrow(0, b, b),
           buf.narrow(0, 2 * b, b * t).view({b, t})};
+}
+
+// ---- the global step's two halves (GlobalIndex.start_global_step /
+// finish_global_step): the same C ABI calls, stream fork and join as the
+// Python orchestration, in one dispatcher hop each. Streams and events
+// arrive as raw handles (0 = everything on the current stream); the
+// caller owns every buffer (found = sa_len, sa_start, sa_end, d_len,
+// d_pos, d_cnt).
+
+void global_start(const at::Tensor& counts, const at::Tensor& token_ids,
+                  const c10::optional<at::Tensor>& sampled,
+                  const c10::optional<at::Tensor>& valid_count,
+                  const c10::optional<at::Tensor>& mask, int64_t limit,
+                  const at::Tensor& sa, const at::Tensor& corpus,
+                  int64_t capacity, const at::Tensor& delta,
+                  int64_t delta_capacity, const at::Tensor& delta_len,
+                  const at::Tensor& caps, const at::Tensor& tails,
+                  const at::Tensor& tail_len, const at::Tensor& row_mask,
+                  at::TensorList found, int64_t max_occ, int64_t s0,
+                  int64_t s1, int64_t ev0, int64_t ev1) {
+  TORCH_CHECK(token_ids.is_cuda() && token_ids.scalar_type() == at::kInt &&
+                  token_ids.dim() == 2 && token_ids.stride(1) == 1,
+              "token_ids must be an int32 CUDA [B, S] tensor");
+  TORCH_CHECK(counts.scalar_type() == at::kInt && counts.is_contiguous(),
+              "counts must be contiguous int32");
+  TORCH_CHECK(found.size() == 6, "found must hold six tensors");
+  const c10::cuda::CUDAGuard guard(token_ids.device());
+  const int64_t b = token_ids.size(0), s = token_ids.size(1);
+  const int32_t p = static_cast<int32_t>(tails.size(1));
+  const int32_t cnum = static_cast<int32_t>(caps.numel());
+  auto cur = reinterpret_cast<cudaStream_t>(
+      c10::cuda::getCurrentCUDAStream(token_ids.device().index()).stream());
+  cudaStream_t st_tails = cur, st_sa = cur, st_delta = cur;
+  if (s0 != 0) {
+    st_tails = st_sa = reinterpret_cast<cudaStream_t>(s0);
+    st_delta = reinterpret_cast<cudaStream_t>(s1);
+    check_cuda(cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev0), cur));
+    check_cuda(cudaStreamWaitEvent(st_tails,
+                                   reinterpret_cast<cudaEvent_t>(ev0), 0));
+  }
+  const int32_t* samp = ptr_or_null<int32_t>(sampled);
+  const int32_t t_cols = sampled.has_value()
+      ? static_cast<int32_t>(sampled->size(1)) : 0;
+  const int32_t* vc = sampled.has_value() ? ptr_or_null<int32_t>(valid_count)
+                                          : nullptr;
+  const uint8_t* m8 = sampled.has_value() ? nullptr
+                                          : ptr_or_null<uint8_t>(mask);
+  check_status("sg_gather_tails_update", sg_gather_tails_update(
+      token_ids.data_ptr<int32_t>(), token_ids.stride(0),
+      static_cast<int32_t>(s), counts.data_ptr<int32_t>(), samp, t_cols, vc,
+      limit, m8, static_cast<int32_t>(b), p, tails.data_ptr<int32_t>(),
+      tail_len.data_ptr<int64_t>(), row_mask.data_ptr<uint8_t>(),
+      reinterpret_cast<sg_stream_t>(st_tails)));
+  if (s0 != 0) {  // the delta scan needs the tails
+    check_cuda(cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev1), st_tails));
+    check_cuda(cudaStreamWaitEvent(st_delta,
+                                   reinterpret_cast<cudaEvent_t>(ev1), 0));
+  }
+  check_status("sg_suffix_match_backoff", sg_suffix_match_backoff(
+      sa.data_ptr<int32_t>(), corpus.data_ptr<int32_t>(), capacity,
+      tails.data_ptr<int32_t>(), static_cast<int32_t>(b), p,
+      tail_len.data_ptr<int64_t>(), p, caps.data_ptr<int64_t>(), cnum,
+      row_mask.data_ptr<uint8_t>(), found[0].data_ptr<int64_t>(),
+      found[1].data_ptr<int64_t>(), found[2].data_ptr<int64_t>(),
+      reinterpret_cast<sg_stream_t>(st_sa)));
+  check_status("sg_delta_match_backoff", sg_delta_match_backoff(
+      delta.data_ptr<int32_t>(), delta_capacity,
+      delta_len.data_ptr<int64_t>(), tails.data_ptr<int32_t>(),
+      static_cast<int32_t>(b), p, tail_len.data_ptr<int64_t>(), p,
+      caps.data_ptr<int64_t>(), cnum, static_cast<int32_t>(max_occ),
+      row_mask.data_ptr<uint8_t>(), found[3].data_ptr<int64_t>(),
+      found[4].data_ptr<int64_t>(), found[5].data_ptr<int64_t>(),
+      reinterpret_cast<sg_stream_t>(st_delta)));
+}
+
+// Returns SG_OK, or SG_ERR_UNSUPPORTED when the fused step does not fit
+// shared memory (the caller then runs the separate steps).
+int64_t global_finish(at::TensorList found, const at::Tensor& row_mask,
+                      const at::Tensor& sa, const at::Tensor& corpus,
+                      int64_t capacity, const at::Tensor& delta,
+                      int64_t delta_capacity, const at::Tensor& delta_len,
+                      int64_t max_occ, int64_t k, bool has_spec,
+                      double spec_factor, double spec_offset,
+                      double min_prob, double alpha,
+                      const at::Tensor& local_score, const at::Tensor& draft,
+                      const at::Tensor& num_valid, int64_t s0, int64_t s1,
+                      int64_t ev2, int64_t ev3) {
+  TORCH_CHECK(found.size() == 6, "found must hold six tensors");
+  const c10::cuda::CUDAGuard guard(draft.device());
+  auto cur = reinterpret_cast<cudaStream_t>(
+      c10::cuda::getCurrentCUDAStream(draft.device().index()).stream());
+  if (s0 != 0) {
+    check_cuda(cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev2),
+                               reinterpret_cast<cudaStream_t>(s0)));
+    check_cuda(cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev3),
+                               reinterpret_cast<cudaStream_t>(s1)));
+    check_cuda(cudaStreamWaitEvent(cur, reinterpret_cast<cudaEvent_t>(ev2), 0));
+    check_cuda(cudaStreamWaitEvent(cur, reinterpret_cast<cudaEvent_t>(ev3), 0));
+  }
+  const int32_t b = static_cast<int32_t>(row_mask.size(0));
+  const int32_t cnum = static_cast<int32_t>(found[0].size(1));
+  const int st = sg_global_draft(
+      found[0].data_ptr<int64_t>(), found[1].data_ptr<int64_t>(),
+      found[2].data_ptr<int64_t>(), found[3].data_ptr<int64_t>(),
+      found[4].data_ptr<int64_t>(), found[5].data_ptr<int64_t>(),
+      sa.data_ptr<int32_t>(), corpus.data_ptr<int32_t>(), capacity,
+      delta.data_ptr<int32_t>(), delta_capacity,
+      delta_len.data_ptr<int64_t>(), b, cnum, static_cast<int32_t>(max_occ),
+      static_cast<int32_t>(k), has_spec ? 1 : 0,
+      static_cast<float>(spec_factor), static_cast<float>(spec_offset),
+      static_cast<float>(min_prob), static_cast<float>(alpha),
+      local_score.data_ptr<float>(), row_mask.data_ptr<uint8_t>(),
+      draft.data_ptr<int32_t>(), num_valid.data_ptr<int32_t>(),
+      reinterpret_cast<sg_stream_t>(cur));
+  if (st == SG_ERR_UNSUPPORTED) return st;
+  check_status("sg_global_draft", st);
+  return SG_OK;
 }
 
 }  // namespace
@@ -223,9 +360,25 @@ TORCH_LIBRARY(suffixgpu_b200, m) {
   m.def(
       "vllm_prepare(Tensor sampled, Tensor? discard, Tensor token_ids, "
       "Tensor num_tokens, int vocab_size) -> Tensor[]");
+  m.def(
+      "global_start(Tensor counts, Tensor token_ids, Tensor? sampled, "
+      "Tensor? valid_count, Tensor? mask, int limit, Tensor sa, "
+      "Tensor corpus, int capacity, Tensor delta, int delta_capacity, "
+      "Tensor delta_len, Tensor caps, Tensor tails, Tensor tail_len, "
+      "Tensor row_mask, Tensor[] found, int max_occ, int s0, int s1, "
+      "int ev0, int ev1) -> ()");
+  m.def(
+      "global_finish(Tensor[] found, Tensor row_mask, Tensor sa, "
+      "Tensor corpus, int capacity, Tensor delta, int delta_capacity, "
+      "Tensor delta_len, int max_occ, int k, bool has_spec, "
+      "float spec_factor, float spec_offset, float min_prob, float alpha, "
+      "Tensor local_score, Tensor draft, Tensor num_valid, int s0, int s1, "
+      "int ev2, int ev3) -> int");
 }
 
 TORCH_LIBRARY_IMPL(suffixgpu_b200, CUDA, m) {
   m.impl("local_draft", &local_draft);
   m.impl("vllm_prepare", &vllm_prepare);
+  m.impl("global_start", &global_start);
+  m.impl("global_finish", &global_finish);
 }

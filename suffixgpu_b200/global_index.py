@@ -26,7 +26,7 @@ from collections import deque
 import torch
 
 from suffixgpu_b200 import ops
-from suffixgpu_b200._lib import call, check, lib, ptr, stream_of
+from suffixgpu_b200._lib import call, check, lib, ptr, stream_of, torch_ops
 
 PAD_TOKEN = torch.iinfo(torch.int32).max
 SEP_TOKEN = -2
@@ -113,6 +113,20 @@ def _serve_builds(jobs: queue.SimpleQueue) -> None:
             return
         job()
         del job  # the job holds the index; do not keep it while idle
+
+
+def _stream_handles(streams):
+    """Raw handles (s0, s1, ev0..ev3) for the global-step operators, or None
+    when they cannot be used: everything on the current stream (no side
+    streams; 0 handles) is fine, side streams need events that exist
+    already (a torch event gets its CUDA event at its first record)."""
+    if streams is None:
+        return (0, 0, 0, 0, 0, 0)
+    s0, s1, ev = streams
+    hs = [e.cuda_event for e in ev]
+    if not all(hs):
+        return None
+    return (s0.cuda_stream, s1.cuda_stream, *hs)
 
 
 class GlobalIndex:
@@ -681,6 +695,17 @@ class GlobalIndex:
                 self._step_bufs[key] = st
         sa_len, sa_start, sa_end, d_len, d_pos, d_cnt = st["found"]
         tails, tail_len, row_mask = st["tails"], st["tail_len"], st["row_mask"]
+        lim = s if limit is None else int(limit)
+        handles = _stream_handles(streams)
+        if handles is not None:
+            # one dispatcher hop: the same three calls and the fork in C++
+            torch_ops().global_start(
+                counts, token_ids, samp, vc, m8, lim, self.sa, self.corpus,
+                self.capacity, self.delta, self.delta_capacity,
+                self.delta_len_t, caps, tails, tail_len, row_mask,
+                st["found"], r, handles[0], handles[1], handles[2],
+                handles[3])
+            return st
         if streams is None:
             s_tails = s_sa = s_delta = stream_of(dev)
         else:
@@ -712,6 +737,23 @@ class GlobalIndex:
         and scored and combined with the local winner in place (global wins
         only on a strictly greater score; proposer.py:305-320)."""
         dev = self.device
+        handles = _stream_handles(streams)
+        if handles is not None and self.k == drafter.k:
+            # join + fused step in one dispatcher hop
+            code = torch_ops().global_finish(
+                pending["found"], pending["row_mask"], self.sa, self.corpus,
+                self.capacity, self.delta, self.delta_capacity,
+                self.delta_len_t, self.max_occurrences, drafter.k,
+                drafter.max_spec_factor is not None,
+                float(drafter.max_spec_factor or 0.0),
+                float(drafter.max_spec_offset),
+                float(drafter.min_token_prob),
+                float(drafter.vote_smoothing_alpha), local["best_score"],
+                local["draft"], local["num_valid"], handles[0], handles[1],
+                handles[4], handles[5])
+            if code == 0:
+                return local["draft"], local["num_valid"]
+            streams = None  # joined already; the separate steps follow
         if streams is not None:
             s0, s1, ev = streams
             cur = torch.cuda.current_stream(dev)

@@ -201,9 +201,14 @@ class SuffixGPUDrafter:
         if not self.parallel_paths:
             return None
         if self._aux is None:
-            self._aux = (torch.cuda.Stream(self.device),
-                         torch.cuda.Stream(self.device),
-                         tuple(torch.cuda.Event() for _ in range(4)))
+            s0 = torch.cuda.Stream(self.device)
+            evs = tuple(torch.cuda.Event() for _ in range(4))
+            if not torch.cuda.is_current_stream_capturing():
+                # give the events their CUDA events now, so the global
+                # step's operators can take their handles
+                for e in evs:
+                    e.record(s0)
+            self._aux = (s0, torch.cuda.Stream(self.device), evs)
         return self._aux
 
     # ------------------------------------------------------------------
