@@ -111,6 +111,12 @@ def test_torch_operator_registers():
     assert "Tensor? out_draft=None, Tensor? out_num_valid=None" in schema
     schema = str(_lib.torch_ops().vllm_prepare.default._schema)
     assert schema.startswith("suffixgpu_b200::vllm_prepare(Tensor sampled")
+    schema = str(_lib.torch_ops().global_start.default._schema)
+    assert schema.startswith("suffixgpu_b200::global_start(Tensor counts")
+    assert schema.endswith("-> ()")
+    schema = str(_lib.torch_ops().global_finish.default._schema)
+    assert schema.startswith("suffixgpu_b200::global_finish(Tensor[] found")
+    assert schema.endswith("-> int")
 
 
 def test_torch_operator_shares_the_process_cxx_runtime():
