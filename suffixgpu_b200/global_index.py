@@ -298,13 +298,10 @@ class GlobalIndex:
         if snap > 0:
             dst[n_active_keep:n_new].copy_(self.delta[:snap])
 
-        # kept active docs (all but the evicted oldest) + absorbed delta docs
-        # (work proportional to the evicted and absorbed docs, not to the
-        # thousands of active ones)
-        new_doc_lens: deque[int] = deque(self.active_doc_lens)
-        for _ in range(evicted):
-            new_doc_lens.popleft()
-        new_doc_lens.extend(self.delta_doc_lens[:absorbed])
+        # kept active docs (all but the evicted oldest) + absorbed delta docs,
+        # applied to the active list at the swap (work proportional to the
+        # evicted and absorbed docs, not to the thousands of active ones)
+        new_doc_lens = (evicted, list(self.delta_doc_lens[:absorbed]))
 
         # Staging owns a copy of the snapshot; compact it out of the delta.
         docs_absorbed = absorbed
@@ -391,12 +388,20 @@ class GlobalIndex:
                     self.staging_sa[m:].copy_(self._arange[m:])
                 torch.cuda.ExternalStream(stream).synchronize()
 
-    def _finish_swap(self, n_new: int, new_doc_lens: deque[int]) -> None:
+    def _finish_swap(self, n_new: int, new_doc_lens) -> None:
+        """new_doc_lens: the new active document lengths, or (evicted,
+        absorbed): drop that many oldest documents and append these."""
         # In-place copies keep the active tensors' storage (graph safety).
         self.corpus.copy_(self.staging_corpus)
         self.sa.copy_(self.staging_sa)
         self.active_len = n_new
-        self.active_doc_lens = new_doc_lens
+        if isinstance(new_doc_lens, tuple):
+            evicted, absorbed = new_doc_lens
+            for _ in range(evicted):
+                self.active_doc_lens.popleft()
+            self.active_doc_lens.extend(absorbed)
+        else:
+            self.active_doc_lens = new_doc_lens
         self._sa_rounds = self._staging_rounds
         self._rebuild_event = None
         self._pending = None
