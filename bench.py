@@ -188,6 +188,51 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
+# device-side timing
+# ---------------------------------------------------------------------------
+# Cycles of the spin kernel that keeps the stream busy while the host
+# records the start event and issues the timed work (about 130 us at
+# 1965 MHz, several times the host's launch latency).
+SPIN_CYCLES = 1 << 18
+
+
+def device_window(run, world: int) -> float:
+    """Device time (ms) of the work ``run()`` enqueues on the current
+    stream. A spin kernel is queued first, so the start event is recorded
+    on a stream that is already busy and ``run()``'s first launch is queued
+    before the spin ends: the host's event-record and launch latency stay
+    outside the window. Barrier and synchronize on both sides."""
+    import torch
+    import torch.distributed as dist
+    stream = torch.cuda.current_stream()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    torch.cuda._sleep(SPIN_CYCLES)
+    e0.record(stream)
+    run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    return e0.elapsed_time(e1)
+
+
+def ranks_ms(ms: float, world: int, dev) -> list[float]:
+    """Every rank's device time, gathered on all ranks (rank order)."""
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return [ms]
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(x.item()) for x in out]
+
+
+# ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
 def run_ours(args):
@@ -260,27 +305,17 @@ def run_ours(args):
 
     clock = ClockSampler(local)
     clock.start()
-    stream = torch.cuda.current_stream()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for _ in range(args.steps // cycle):
-        full.replay()
-    if part is not None:
-        part.replay()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+
+    def replays():
+        for _ in range(args.steps // cycle):
+            full.replay()
+        if part is not None:
+            part.replay()
+
+    ms = device_window(replays, world)
     clocks = clock.stop()
-    ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_ranks = ranks_ms(ms, world, dev)
+    ms_max = max(ms_ranks)
 
     # algorithmic bytes over the timed steps (the reset node is outside)
     seq = step_seq(args.steps)
@@ -304,6 +339,8 @@ def run_ours(args):
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": ms_max / args.steps,
+            "ms_per_step_ranks": [m / args.steps for m in ms_ranks],
+            "ms_per_step_median": statistics.median(ms_ranks) / args.steps,
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
@@ -570,23 +607,13 @@ def run_sharded(args, dev, world: int, rank: int) -> dict | None:
     torch.cuda.synchronize()
     reps_needed = max(1, steps // cycle)
     steps = reps_needed * min(steps, cycle)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(reps_needed):
-        graph.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms, load_s], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max, load_max = float(t[0].item()), float(t[1].item())
+    def replays():
+        for _ in range(reps_needed):
+            graph.replay()
+
+    ms_ranks = ranks_ms(device_window(replays, world), world, dev)
+    ms_max = max(ms_ranks)
+    load_max = max(ranks_ms(load_s, world, dev))
     del graph
     if rank != 0:
         return None
@@ -595,6 +622,7 @@ def run_sharded(args, dev, world: int, rank: int) -> dict | None:
             "value": world * b * steps / (ms_max * 1e-3), "unit": "rows/s",
             "n_gpus": world, "rows_per_gpu": b, "steps": steps,
             "ms_per_step": ms_max / steps, "scaling": "weak",
+            "ms_per_step_ranks": [m / steps for m in ms_ranks],
             "corpus_tokens": int(d.global_index.active_len),
             "load_s": load_max,
             "workload": "config5: 128 rows x S=16384 per GPU, k=32, P=64, "

@@ -129,9 +129,31 @@ typedef struct sg_local_outputs {
  * Propose mode (sampled == NULL): counts are num_tokens and rows draft
  * where mask[b] != 0.
  * Rows must fit in shared memory: S <= ~40k tokens on B200.
+ * Failure: a row whose bulk load into shared memory does not land within
+ * the kernel's bounded wait drafts nothing (draft all -1, num_valid 0,
+ * row_mask 0; the update still happens) and sets SG_DEVERR_WAIT in the
+ * device error word (sg_device_error). Never expected on a healthy GPU.
  */
 int sg_local_draft(const sg_draft_params* params, const sg_local_inputs* in,
                    const sg_local_outputs* out, sg_stream_t stream);
+
+/* ---- device-side failures (no reference counterpart: the reference has
+ * no bounded waits) ------------------------------------------------------- */
+#define SG_DEVERR_WAIT 1u /* a bounded wait of sg_local_draft ran out */
+
+/* Reads the current device's error word (bits SG_DEVERR_*, 0 when no
+ * kernel has failed since the last clear) into *bits; clear != 0 resets it.
+ * Synchronises `stream`: call it off the hot path (a health check, a test).
+ * The word is process-wide per device. */
+int sg_device_error(uint32_t* bits, int clear, sg_stream_t stream);
+
+/* Test hook: the number of polls of sg_local_draft's first wait for a
+ * row's bulk load; 0 makes that wait give up at once, a negative value
+ * restores the default (2^22). A small bound lets a test make the wait run
+ * out on purpose; the kernel still waits for the copy in flight with the
+ * default bound before it exits. Applies to the launches that follow,
+ * process-wide. Returns the previous bound. */
+int sg_set_wait_polls(int polls);
 
 /* ---- reference operator layer (suffix_gpu/triton_kernels.py) ----------- */
 
@@ -193,7 +215,10 @@ int sg_vllm_prepare(const int32_t* sampled, int64_t sampled_stride,
 
 /* ---- suffix array (suffix_gpu/suffix_array.py) -------------------------- */
 
-/* Workspace bytes sg_build_suffix_array needs for n tokens (~36 n). */
+/* Workspace bytes sg_build_suffix_array needs for n tokens (about 54 n:
+ * two 8-byte key and two 4-byte value buffers, ranks, two active lists,
+ * the large-group key / value / position lists and flags, plus per-tile
+ * digit counts). */
 size_t sg_suffix_array_workspace_size(int64_t n);
 
 /* build_suffix_array (suffix_array.py:15-63): sa_out[0..n) = start
@@ -213,13 +238,17 @@ int sg_build_suffix_array(const int32_t* tokens, int64_t n, int32_t* sa_out,
  * cannot allocate (an engine that has reserved all GPU memory up front, a
  * plugin host that only passes input and output buffers). No counterpart in
  * the reference. The workspace is an 8 MiB static __device__ array inside
- * this library (held by every GPU that loads it), so n is limited to about
- * 231 thousand tokens; larger n returns SG_ERR_UNSUPPORTED without
- * launching anything. The first call on a device looks up the array's
- * device address (cudaGetSymbolAddress). All calls share the array: calls
- * whose work overlaps on the GPU (other streams, other host threads) race
- * and must be serialised by the caller. Synchronises `stream` like
- * sg_build_suffix_array. */
+ * this library (held by every GPU that loads it), so n is limited to the
+ * largest n with sg_suffix_array_workspace_size(n) <= 8 MiB (about 155
+ * thousand tokens); larger n returns SG_ERR_UNSUPPORTED without launching
+ * anything. The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress). All calls share the array: calls whose work
+ * overlaps on the GPU (other streams, other host threads) race and must be
+ * serialised by the caller. Synchronises `stream` like
+ * sg_build_suffix_array. Device memory is never allocated; the first
+ * suffix-array build of the process (through either entry point) may make
+ * one 4 KiB page-locked host allocation (cudaHostAlloc) for the per-round
+ * counts, and falls back to a stack slot when that fails. */
 int sg_build_suffix_array_noalloc(const int32_t* tokens, int64_t n,
                                   int32_t* sa_out, int32_t* rounds_out,
                                   sg_stream_t stream);
@@ -272,6 +301,25 @@ int sg_suffix_match_backoff(const int32_t* sa, const int32_t* corpus,
                             int64_t* out_end, sg_stream_t stream);
 
 /* ---- global index (suffix_gpu/global_index.py) --------------------------- */
+
+/* GlobalIndex.append_documents' device writes (global_index.py:86-108: per
+ * document a slice copy, a SEP write and a length fill), batched: document
+ * i (docs[i], lens[i] int32 tokens, device memory) is written to
+ * buf[pos_i .. pos_i + lens[i]) followed by SEP = -2, with pos_0 = start and
+ * pos_{i+1} = pos_i + lens[i] + 1; then *len_out (device int64, may be
+ * NULL) = the end of the last document's SEP. One launch per 32 documents;
+ * docs and lens are host arrays read during the call. Requires the end
+ * <= capacity (else SG_ERR_INVALID, nothing launched). */
+int sg_append_documents(int32_t* buf, int64_t capacity, int64_t start,
+                        const int32_t* const* docs, const int64_t* lens,
+                        int32_t n_docs, int64_t* len_out, sg_stream_t stream);
+
+/* The delta's compaction (global_index.py:127-131, 191-199: the documents
+ * before `from` left it): buf[0 .. count) = buf[from .. from + count)
+ * (overlapping move, exact), then *len_out (device int64, may be NULL) =
+ * count. One launch. */
+int sg_delta_compact(int32_t* buf, int64_t capacity, int64_t from,
+                     int64_t count, int64_t* len_out, sg_stream_t stream);
 
 /* GlobalIndex._delta_match_backoff (global_index.py:465-546) over the delta
  * buffer; delta_len is a device int64 scalar. Outputs: out_len [B, C]

@@ -105,6 +105,11 @@ _SIGS: dict[str, list] = {
                              c_int32, c_int32, c_int32, c_float, c_float,
                              c_void_p, c_void_p, c_void_p, c_void_p,
                              c_void_p],
+    "sg_append_documents": [c_void_p, c_int64, c_int64, c_void_p, c_void_p,
+                            c_int32, c_void_p, c_void_p],
+    "sg_delta_compact": [c_void_p, c_int64, c_int64, c_int64, c_void_p,
+                         c_void_p],
+    "sg_device_error": [POINTER(ctypes.c_uint32), c_int, c_void_p],
     "sg_global_combine": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                           c_void_p, c_void_p, c_int32, c_int32, c_int32,
                           c_void_p],
@@ -144,6 +149,7 @@ def lib() -> ctypes.CDLL:
 # entry points with non-int return types: name -> (restype, argtypes)
 _SIGS_EXTRA: dict[str, tuple] = {
     "sg_suffix_array_workspace_size": (c_size_t, [c_int64]),
+    "sg_set_wait_polls": (c_int, [c_int]),
     "sg_suffix_array_append_workspace_size": (c_size_t, [c_int64]),
 }
 

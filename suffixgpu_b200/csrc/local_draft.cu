@@ -33,6 +33,8 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "sg_common.cuh"
 #include "sg_vote.cuh"
 
@@ -78,9 +80,19 @@ struct LocalLayout {
 struct LocalArgs {
   sg_draft_params p;
   int n_cand;  // candidates that can be nonzero: 2^c <= S, capped at kMaxCand
+  int wait_polls;  // bound of the row-load wait (sg_set_wait_polls)
   sg_local_inputs in;
   sg_local_outputs out;
 };
+
+// Device error word of this library's draft kernels (one per device that
+// loads the library): bits OR-ed in by kernels, read and cleared by
+// sg_device_error. Set only on failures, so it costs nothing otherwise.
+static __device__ unsigned int g_device_error;
+
+// Bound of the first wait for a row's bulk load, in polls. Lowered only by
+// tests (sg_set_wait_polls) to make that wait run out on purpose.
+static std::atomic<int> g_wait_polls{kWaitPolls};
 
 __device__ __forceinline__ long long spec_cap(const sg_draft_params& p,
                                               int len) {
@@ -277,19 +289,29 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
   // (disjoint from the bulk copy's shared-memory range)
   for (int i = nal + t; i < nload; i += kLocalThreads) tok_s[i] = row[i];
   bool timed_out = false;
-  if (nal > 0 && !mbar_wait(bar, 0)) {
+  if (nal > 0 && !mbar_wait(bar, 0, a.wait_polls)) {
     // A bulk copy of resident memory always lands; should the bound ever
-    // run out, wait once more for the copy in flight, then report the row
-    // as failed (num_valid = -1) instead of drafting from partial data.
-    timed_out = !mbar_wait(bar, 0);
+    // run out, the row drafts nothing (zero drafts, not partial data) and
+    // the device error word says so. The copy in flight is waited for
+    // (with the full bound) before the block's shared memory is given up.
+    timed_out = true;
+    atomicOr(&g_device_error, kDevErrWait);
+    mbar_wait(bar, 0);
   }
   if (__syncthreads_or(timed_out)) {
     for (int d = t; d < K; d += kLocalThreads)
       a.out.draft[static_cast<long long>(b) * K + d] = -1;
     if (t == 0) {
-      a.out.num_valid[b] = -1;
-      if (srow) a.out.new_counts[b] = static_cast<int32_t>(q);
+      a.out.num_valid[b] = 0;
+      if (a.out.best_score) a.out.best_score[b] = 0.0f;
+      if (a.out.best_len) a.out.best_len[b] = 0;
+      if (a.out.best_occ) a.out.best_occ[b] = 0;
+      if (a.out.row_mask) a.out.row_mask[b] = 0;
     }
+    // the update does not depend on the load: it still happens
+    if (warp == 0 && srow)
+      scatter_to_row(row, lane, T, srow, my_samp, s_base, s_cnt, S, q,
+                     a.out.new_counts + b);
     return;
   }
   if (warp == 0 && mask) {
@@ -662,6 +684,7 @@ extern "C" int sg_local_draft(const sg_draft_params* params,
   if (nc < 1) nc = 1;
   if (nc > kMaxCand) return SG_ERR_UNSUPPORTED;
   a.n_cand = nc;
+  a.wait_polls = g_wait_polls.load(std::memory_order_relaxed);
   a.in = *in;
   a.out = *out;
   const LocalLayout L(p.seq_len, p.max_pattern_len, nc, p.max_occurrences, p.k);
@@ -669,4 +692,30 @@ extern "C" int sg_local_draft(const sg_draft_params* params,
   if (p.max_occurrences <= 128) return launch_local<4>(a, L.total, st);
   if (p.max_occurrences <= 256) return launch_local<8>(a, L.total, st);
   return launch_local<32>(a, L.total, st);
+}
+
+extern "C" int sg_set_wait_polls(int polls) {
+  return sg::g_wait_polls.exchange(polls < 0 ? sg::kWaitPolls : polls);
+}
+
+extern "C" int sg_device_error(uint32_t* bits, int clear, sg_stream_t stream) {
+  if (!bits) return SG_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, sg::g_device_error,
+                                            sizeof(v), 0,
+                                            cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && clear && v) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbolAsync(sg::g_device_error, &zero, sizeof(zero), 0,
+                                cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  }
+  if (e != cudaSuccess) {
+    sg::set_cuda_error(e);
+    return SG_ERR_CUDA;
+  }
+  *bits = v;
+  return SG_OK;
 }

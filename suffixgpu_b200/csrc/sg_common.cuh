@@ -145,11 +145,16 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem,
       : "memory");
 }
 
-// Bounded wait for phase `parity` of `bar`. Returns false if the bound ran
-// out (the caller records an error and keeps going).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Polls of a bounded mbarrier wait: far beyond any bulk copy of resident
+// memory (a copy lands within microseconds; 2^22 polls take milliseconds).
+constexpr int kWaitPolls = 1 << 22;
+
+// Bounded wait for phase `parity` of `bar`: at most `polls` polls. Returns
+// false if the bound ran out (the caller records an error and keeps going).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          int polls = kWaitPolls) {
   const uint32_t addr = smem_u32(bar);
-  for (int it = 0; it < (1 << 22); ++it) {
+  for (int it = 0; it < polls; ++it) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -176,8 +181,8 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
-// Device-side error word: kernels OR error bits into it; the host reads it
-// back in tests. Bit 0: a bounded wait timed out.
-constexpr int kDevErrWait = 1;
+// Bits of the device error word (sg_device_error): a bounded wait of the
+// local draft kernel ran out.
+constexpr unsigned kDevErrWait = SG_DEVERR_WAIT;
 
 }  // namespace sg

@@ -109,6 +109,11 @@ class ShardedSuffixDrafter(SuffixGPUDrafter):
         if all_docs:
             self.global_index.append_documents(all_docs)
 
+    def _append_rows(self, token_ids: torch.Tensor, rows: list[int],
+                     lengths: list[int]) -> None:
+        self._append_docs([token_ids[r, :ln]
+                           for r, ln in zip(rows, lengths) if ln > 0])
+
     def load_documents(self, docs: list[torch.Tensor]) -> None:
         """Bulk-load documents that every rank holds (the same list on
         every rank, e.g. generated from a shared seed): no exchange."""

@@ -2,31 +2,37 @@
 plus an append-only delta buffer), the reference's GlobalIndex
 (suffix_gpu/global_index.py:41-553) on the sm_100a kernels.
 
-The host-side bookkeeping (document lengths, eviction, snapshot, delta
-compaction, rebuild trigger and swap) follows the reference step by step;
-the device work goes through the C ABI: sg_build_suffix_array for the
-staging SA, sg_suffix_match_backoff + sg_delta_match_backoff +
-sg_global_candidates for queries. The active corpus/SA keep their storage
-across swaps (in-place copies), so captured CUDA graphs stay valid.
+State and rules are the reference's (what a caller can observe: corpus,
+suffix array, delta, document lengths, when rebuilds happen and what they
+evict or absorb); the implementation is this package's. Document lengths
+live in two ``DocLedger`` queues of running totals (doc_ledger.py), so a
+rebuild's eviction and absorption come from binary searches, and the
+device writes of a harvest are one C-ABI call (sg_append_documents: all
+documents and their SEPs in one launch, the device length included), as
+is the delta's compaction (sg_delta_compact). Queries go through
+sg_suffix_match_backoff + sg_delta_match_backoff + the fused global step.
+The active corpus / SA keep their storage across swaps (in-place copies),
+so captured CUDA graphs stay valid.
 
-Rebuilds run synchronously (the reference's behaviour on CPU and without a
-rebuild stream). With ``rebuild_stream`` set, the staging build runs on
-that stream from a background host thread and the swap happens at the
-first ``poll_rebuild`` after it has finished, as in the reference.
+Rebuilds run synchronously without a rebuild stream (the reference's
+behaviour on CPU and without one). With ``rebuild_stream`` set, the
+staging build runs on that stream from a background host thread and the
+swap happens at the first ``poll_rebuild`` after it has finished, as in the
+reference.
 """
 
 from __future__ import annotations
 
+import ctypes
 import queue
 import threading
 import time
 import weakref
-from collections import deque
-
 import torch
 
 from suffixgpu_b200 import ops
 from suffixgpu_b200._lib import call, check, lib, ptr, stream_of, torch_ops
+from suffixgpu_b200.doc_ledger import DocLedger, plan_bulk_load, plan_snapshot
 
 PAD_TOKEN = torch.iinfo(torch.int32).max
 SEP_TOKEN = -2
@@ -36,56 +42,6 @@ _UNSUPPORTED = 4  # SG_ERR_UNSUPPORTED
 # comparisons can run that deep (on a corpus of exactly repeated 256K-token
 # stretches the merge took 12 ms against 4.2 ms for a full build).
 _APPEND_MAX_ROUNDS = 12
-
-
-def plan_bulk_load(active_doc_lens, active_len: int, new_doc_lens,
-                   capacity: int):
-    """Host bookkeeping of a bulk load: the documents of ``new_doc_lens``
-    (each length counting its SEP) are appended to an otherwise empty delta
-    and rebuilds run (global_index.py:147-223 rules: evict the oldest whole
-    active documents until active + delta fit, absorb the oldest whole
-    delta documents that fit) until the delta is empty. Returns
-    (keep_tokens, first_new, n_new_docs, rebuilds): the final corpus is the
-    last ``keep_tokens`` tokens of the current active corpus followed by
-    new documents ``first_new .. first_new + n_new_docs - 1``."""
-    act = list(active_doc_lens)       # lengths of the current corpus docs
-    src = [0] * len(act)              # 0 = old active doc, 1 = new doc
-    idx = list(range(len(act)))       # index within its source
-    delta = list(range(len(new_doc_lens)))
-    dlen = sum(new_doc_lens)
-    alen = active_len
-    rebuilds = 0
-    while delta:
-        keep = 0
-        drop = 0
-        for ln in act:
-            if alen - keep + dlen <= capacity:
-                break
-            keep += ln
-            drop += 1
-        n_keep = alen - keep
-        room = capacity - n_keep
-        take = 0
-        acc = 0
-        for j in delta:
-            if acc + new_doc_lens[j] <= min(dlen, room):
-                acc += new_doc_lens[j]
-                take += 1
-            else:
-                break
-        if n_keep + acc == 0:
-            break  # nothing fits (a document longer than the capacity)
-        act = act[drop:] + [new_doc_lens[j] for j in delta[:take]]
-        src = src[drop:] + [1] * take
-        idx = idx[drop:] + delta[:take]
-        delta = delta[take:]
-        dlen -= acc
-        alen = n_keep + acc
-        rebuilds += 1
-    old = [ln for ln, s in zip(act, src) if s == 0]
-    new = [i for i, s in zip(idx, src) if s == 1]
-    first_new = new[0] if new else len(new_doc_lens)
-    return sum(old), first_new, len(new), rebuilds
 
 
 class _ThreadEvent:
@@ -158,11 +114,13 @@ class GlobalIndex:
         self.delta = torch.zeros(delta_capacity, dtype=torch.int32,
                                  device=dev)
         self.delta_len_t = torch.zeros((), dtype=torch.int64, device=dev)
-        self._sep1 = torch.full((1,), SEP_TOKEN, dtype=torch.int32, device=dev)
         self.active_len = 0
         self.delta_len = 0
-        self.active_doc_lens: deque[int] = deque()
-        self.delta_doc_lens: list[int] = []
+        # document lengths (each counting its SEP), oldest first
+        self.active_doc_lens = DocLedger()
+        self.delta_doc_lens = DocLedger()
+        # a background rebuild in flight: its completion flag, and what the
+        # swap applies (corpus length, evicted documents, absorbed lengths)
         self._rebuild_event = None
         self._pending = None
         # one long-lived build thread per index (started on first use): a
@@ -193,154 +151,163 @@ class GlobalIndex:
     # ------------------------------------------------------------------
     def append_documents(self, docs: list[torch.Tensor]) -> None:
         """Append finished-response token tensors to the delta, each
-        followed by one SEP_TOKEN (recorded doc lengths include it). The
-        device writes of consecutive documents go out as one copy."""
-        pending: list[torch.Tensor] = []
-        start = self.delta_len
-
-        def flush():
-            nonlocal pending, start
-            if pending:
-                blob = torch.cat(pending)
-                self.delta[start:start + blob.numel()].copy_(blob)
-                pending = []
-            self.delta_len_t.fill_(self.delta_len)
-            start = self.delta_len
-
+        followed by one SEP_TOKEN (recorded lengths include it). A document
+        longer than the delta keeps its newest delta_capacity - 1 tokens."""
+        held = []
         for doc in docs:
-            doc = doc.to(self.device).to(torch.int32).reshape(-1)
-            n = doc.shape[0]
-            if n == 0:
-                continue
-            if n + 1 > self.delta_capacity:
-                doc = doc[-(self.delta_capacity - 1):]
-                n = doc.shape[0]
-            if self.delta_len + n + 1 > self.delta_capacity:
-                flush()
+            d = doc.reshape(-1)
+            if (d.device != self.device or d.dtype != torch.int32
+                    or not d.is_contiguous()):
+                d = d.to(device=self.device, dtype=torch.int32).contiguous()
+            if d.numel():
+                held.append(d)  # alive until its copy is enqueued
+        self._ingest([(d.data_ptr(), d.numel()) for d in held])
+
+    def append_rows(self, token_ids: torch.Tensor, rows: list[int],
+                    lengths: list[int]) -> None:
+        """append_documents of ``token_ids[r, :length]`` for each row r,
+        without slicing on the host (harvest_finished's documents)."""
+        if token_ids.dtype != torch.int32 or token_ids.device != self.device \
+                or token_ids.stride(1) != 1:
+            self.append_documents([token_ids[r, :ln]
+                                   for r, ln in zip(rows, lengths)])
+            return
+        base = token_ids.data_ptr()
+        pitch = 4 * token_ids.stride(0)
+        width = token_ids.shape[1]
+        self._ingest([(base + pitch * r, min(ln, width))
+                      for r, ln in zip(rows, lengths) if ln > 0])
+
+    def _ingest(self, docs: list[tuple[int, int]]) -> None:
+        """Documents given as (device address, tokens) go after the delta's
+        documents. Writes are batched; a document that does not fit first
+        makes room (a rebuild, or dropping the oldest documents while one is
+        in flight), and the batch before it is written before that."""
+        cap = self.delta_capacity
+        batch: list[tuple[int, int]] = []
+        start = self.delta_len
+        for addr, n in docs:
+            if n + 1 > cap:  # keep the newest cap - 1 tokens
+                addr += 4 * (n - (cap - 1))
+                n = cap - 1
+            if self.delta_len + n + 1 > cap:
+                self._write_docs(self.delta, cap, start, batch)
+                batch = []
                 self._make_room(n + 1)
                 start = self.delta_len
-            pending.append(doc)
-            pending.append(self._sep1)
+            batch.append((addr, n))
             self.delta_len += n + 1
             self.delta_doc_lens.append(n + 1)
-        flush()
+        self._write_docs(self.delta, cap, start, batch)
         self.maybe_rebuild()
 
+    def _write_docs(self, buf: torch.Tensor, capacity: int, start: int,
+                    docs: list[tuple[int, int]], set_len: bool = True
+                    ) -> None:
+        """One sg_append_documents call: docs (and SEPs) from ``start``
+        on; with set_len the delta's device length follows."""
+        if not docs:
+            return
+        n = len(docs)
+        addrs = (ctypes.c_void_p * n)(*(a for a, _ in docs))
+        lens = (ctypes.c_int64 * n)(*(ln for _, ln in docs))
+        call("sg_append_documents", buf.data_ptr(), capacity, start, addrs,
+             lens, n, ptr(self.delta_len_t) if set_len else None,
+             stream_of(self.device))
+
     def _make_room(self, needed: int) -> None:
+        """Room for ``needed`` more delta tokens: a rebuild absorbs the
+        delta; while one is in flight (its staging buffers busy) the
+        oldest delta documents are dropped instead."""
         self.poll_rebuild()
         if self._rebuild_event is None:
             self._launch_rebuild()
-        if self.delta_len + needed <= self.delta_capacity:
-            return
-        # A rebuild is in flight (staging buffers busy): drop oldest docs.
-        self._drop_oldest_docs(self.delta_len + needed - self.delta_capacity)
+        short = self.delta_len + needed - self.delta_capacity
+        if short > 0:
+            n = self.delta_doc_lens.count_covering(short)
+            self._shift_delta(n)
 
-    def _drop_oldest_docs(self, drop: int) -> None:
-        acc = 0
-        docs_dropped = 0
-        for ln in self.delta_doc_lens:
-            if acc >= drop:
-                break
-            acc += ln
-            docs_dropped += 1
-        remaining = self.delta_len - acc
-        if remaining > 0:
-            self.delta[:remaining] = self.delta[acc:self.delta_len].clone()
-        self.delta_len = remaining
-        self.delta_len_t.fill_(remaining)
-        self.delta_doc_lens = self.delta_doc_lens[docs_dropped:]
+    def _shift_delta(self, docs: int) -> None:
+        """The ``docs`` oldest delta documents leave the delta: the rest
+        moves to its front (one launch, device length included)."""
+        gone = self.delta_doc_lens.oldest_tokens(docs)
+        self.delta_doc_lens.drop_oldest(docs)
+        left = self.delta_len - gone
+        call("sg_delta_compact", ptr(self.delta), self.delta_capacity, gone,
+             left, ptr(self.delta_len_t), stream_of(self.device))
+        self.delta_len = left
 
     # ------------------------------------------------------------------
     # rebuild (global_index.py:138-253)
     # ------------------------------------------------------------------
     def maybe_rebuild(self) -> None:
-        """Kick off a rebuild when the delta grew past the threshold."""
+        """A rebuild starts once the delta holds rebuild_threshold tokens
+        and none is in flight."""
         self.poll_rebuild()
-        if self._rebuild_event is not None or self.delta_len == 0:
-            return
-        if self.delta_len < self.rebuild_threshold:
-            return
-        self._launch_rebuild()
+        if self._rebuild_event is None and self.delta_len \
+                and self.delta_len >= self.rebuild_threshold:
+            self._launch_rebuild()
 
     def _launch_rebuild(self) -> None:
+        """Snapshot (plan_snapshot: kept corpus + absorbed delta documents)
+        into the staging buffers, absorbed documents out of the delta at
+        once, then the staging SA build, synchronous or in the background;
+        the swap applies the plan to the active state."""
         if self._rebuild_event is not None:
             return
-        # Evict oldest whole docs until the snapshot fits into capacity.
-        keep_start = 0
-        evicted = 0
-        for ln in self.active_doc_lens:
-            if self.active_len - keep_start + self.delta_len \
-                    <= self.capacity:
-                break
-            keep_start += ln
-            evicted += 1
-        n_active_keep = self.active_len - keep_start
-        snap = min(self.delta_len, self.capacity - n_active_keep)
-        # Clamp the snapshot to a whole-doc boundary in the delta.
-        acc = 0
-        absorbed = 0
-        for ln in self.delta_doc_lens:
-            if acc + ln <= snap:
-                acc += ln
-                absorbed += 1
-            else:
-                break
-        snap = acc
-        n_new = n_active_keep + snap
+        plan = plan_snapshot(self.active_doc_lens, self.delta_doc_lens,
+                             self.capacity)
+        kept = self.active_len - plan.evict_tokens
+        n_new = kept + plan.absorb_tokens
         if n_new == 0:
             return
-
-        dst = self.staging_corpus
-        dst.fill_(PAD_TOKEN)
-        if n_active_keep > 0:
-            dst[:n_active_keep].copy_(
-                self.corpus[keep_start:self.active_len])
-        if snap > 0:
-            dst[n_active_keep:n_new].copy_(self.delta[:snap])
-
-        # kept active docs (all but the evicted oldest) + absorbed delta docs,
-        # applied to the active list at the swap (work proportional to the
-        # evicted and absorbed docs, not to the thousands of active ones)
-        new_doc_lens = (evicted, list(self.delta_doc_lens[:absorbed]))
-
-        # Staging owns a copy of the snapshot; compact it out of the delta.
-        docs_absorbed = absorbed
-        remaining = self.delta_len - snap
-        if remaining > 0:
-            self.delta[:remaining] = self.delta[snap:self.delta_len].clone()
-        self.delta_len = remaining
-        self.delta_len_t.fill_(remaining)
-        self.delta_doc_lens = self.delta_doc_lens[docs_absorbed:]
-
-        # Build over the real prefix plus one sentinel column.
+        self._stage(plan.evict_tokens, kept, plan.absorb_tokens)
+        absorbed = self.delta_doc_lens.oldest_lengths(plan.absorb_docs)
+        if plan.absorb_docs:
+            self._shift_delta(plan.absorb_docs)
+        # the SA covers the real tokens plus one sentinel column
         m = min(n_new + 1, self.capacity)
-        plan = self._build_plan(m, keep_start, n_active_keep)
-        if self.rebuild_stream is not None:
-            self.rebuild_stream.wait_stream(
-                torch.cuda.current_stream(self.device))
-            ev = _ThreadEvent()
-            self._pending = (n_new, new_doc_lens)
-            self._rebuild_event = ev
+        build = self._build_plan(m, plan.evict_tokens, kept)
+        swap = (n_new, plan.evict_docs, absorbed)
+        if self.rebuild_stream is None:
+            self._build_staging_sa(self.staging_corpus, m, None, build)
+            self._finish_swap(*swap)
+            return
+        self.rebuild_stream.wait_stream(
+            torch.cuda.current_stream(self.device))
+        ev = _ThreadEvent()
+        self._pending = swap
+        self._rebuild_event = ev
 
-            def work():
-                try:
-                    with torch.cuda.device(self.device):
-                        self._build_staging_sa(
-                            dst, m, self.rebuild_stream.cuda_stream, plan)
-                except BaseException as e:  # surfaced at poll time
-                    ev.error = e
-                ev.set()
+        def work():
+            try:
+                with torch.cuda.device(self.device):
+                    self._build_staging_sa(
+                        self.staging_corpus, m,
+                        self.rebuild_stream.cuda_stream, build)
+            except BaseException as e:  # surfaced at poll time
+                ev.error = e
+            ev.set()
 
-            if self._worker is None:
-                self._jobs = queue.SimpleQueue()
-                self._worker = threading.Thread(
-                    target=_serve_builds, args=(self._jobs,), daemon=True)
-                self._worker.start()
-                weakref.finalize(self, self._jobs.put, None)
-            self._jobs.put(work)
-        else:
-            self._build_staging_sa(dst, m, None, plan)
-            self._finish_swap(n_new, new_doc_lens)
+        if self._worker is None:
+            self._jobs = queue.SimpleQueue()
+            self._worker = threading.Thread(
+                target=_serve_builds, args=(self._jobs,), daemon=True)
+            self._worker.start()
+            weakref.finalize(self, self._jobs.put, None)
+        self._jobs.put(work)
+
+    def _stage(self, evicted: int, kept: int, absorbed: int) -> None:
+        """staging corpus = active corpus[evicted : evicted + kept], then
+        delta[:absorbed], then PAD up to the capacity."""
+        dst = self.staging_corpus
+        n_new = kept + absorbed
+        if kept:
+            dst[:kept].copy_(self.corpus[evicted:evicted + kept])
+        if absorbed:
+            dst[kept:n_new].copy_(self.delta[:absorbed])
+        if n_new < self.capacity:
+            dst[n_new:].fill_(PAD_TOKEN)
 
     def _build_plan(self, m: int, evicted: int, kept: int):
         """How to build a staging snapshot of m tokens whose first `kept`
@@ -388,20 +355,17 @@ class GlobalIndex:
                     self.staging_sa[m:].copy_(self._arange[m:])
                 torch.cuda.ExternalStream(stream).synchronize()
 
-    def _finish_swap(self, n_new: int, new_doc_lens) -> None:
-        """new_doc_lens: the new active document lengths, or (evicted,
-        absorbed): drop that many oldest documents and append these."""
-        # In-place copies keep the active tensors' storage (graph safety).
+    def _finish_swap(self, n_new: int, evicted_docs: int,
+                     new_lens) -> None:
+        """The staging pair becomes the active one: in-place copies keep
+        the active tensors' storage (graph safety); the oldest
+        ``evicted_docs`` active documents leave the ledger and ``new_lens``
+        join it."""
         self.corpus.copy_(self.staging_corpus)
         self.sa.copy_(self.staging_sa)
         self.active_len = n_new
-        if isinstance(new_doc_lens, tuple):
-            evicted, absorbed = new_doc_lens
-            for _ in range(evicted):
-                self.active_doc_lens.popleft()
-            self.active_doc_lens.extend(absorbed)
-        else:
-            self.active_doc_lens = new_doc_lens
+        self.active_doc_lens.drop_oldest(evicted_docs)
+        self.active_doc_lens.extend(new_lens)
         self._sa_rounds = self._staging_rounds
         self._rebuild_event = None
         self._pending = None
@@ -421,8 +385,7 @@ class GlobalIndex:
                 self._pending = None
                 raise RuntimeError("background suffix-array build failed") \
                     from err
-            n_new, new_doc_lens = self._pending
-            self._finish_swap(n_new, new_doc_lens)
+            self._finish_swap(*self._pending)
 
     # ------------------------------------------------------------------
     # bulk load and persistence (no reference counterpart; the reference
@@ -438,46 +401,32 @@ class GlobalIndex:
         if self.delta_len:
             raise ValueError("load_documents needs an empty delta")
         cap = self.capacity
-        docs = [d.to(self.device).to(torch.int32).reshape(-1) for d in docs]
-        docs = [d[-(cap - 1):] for d in docs if d.numel() > 0]
+        docs = [d.reshape(-1).to(device=self.device,
+                                 dtype=torch.int32).contiguous()[-(cap - 1):]
+                for d in docs if d.numel() > 0]
         if not docs:
             return
         new_lens = [int(d.numel()) + 1 for d in docs]
-        keep, first, count, rounds = plan_bulk_load(
-            self.active_doc_lens, self.active_len, new_lens, cap)
-        if rounds == 0:
+        bp = plan_bulk_load(self.active_doc_lens, new_lens, cap)
+        if bp.rebuilds == 0:
             return
-        offs = [0]
-        for ln in new_lens:
-            offs.append(offs[-1] + ln)
-        n_tail = offs[first + count] - offs[first]
-        n_new = keep + n_tail
+        keep = bp.keep_tokens
+        chosen = docs[bp.first_new:bp.first_new + bp.new_docs]
+        n_new = keep + sum(new_lens[bp.first_new:bp.first_new + bp.new_docs])
         dst = self.staging_corpus
-        dst.fill_(PAD_TOKEN)
-        if keep > 0:
-            dst[:keep].copy_(self.corpus[self.active_len - keep:self.active_len])
-        if count:
-            sep = torch.full((1,), SEP_TOKEN, dtype=torch.int32,
-                             device=self.device)
-            parts = []
-            for d in docs[first:first + count]:
-                parts.append(d)
-                parts.append(sep)
-            dst[keep:n_new].copy_(torch.cat(parts))
-        new_doc_lens: deque[int] = deque()
-        acc = 0
-        kept_old = []
-        for ln in reversed(self.active_doc_lens):
-            if acc >= keep:
-                break
-            kept_old.append(ln)
-            acc += ln
-        new_doc_lens.extend(reversed(kept_old))
-        new_doc_lens.extend(new_lens[first:first + count])
+        if keep:
+            dst[:keep].copy_(
+                self.corpus[self.active_len - keep:self.active_len])
+        self._write_docs(dst, cap, keep,
+                         [(d.data_ptr(), d.numel()) for d in chosen],
+                         set_len=False)
+        if n_new < cap:
+            dst[n_new:].fill_(PAD_TOKEN)
         m = min(n_new + 1, cap)
-        plan = self._build_plan(m, self.active_len - keep, keep)
-        self._build_staging_sa(dst, m, None, plan)
-        self._finish_swap(n_new, new_doc_lens)
+        build = self._build_plan(m, self.active_len - keep, keep)
+        self._build_staging_sa(dst, m, None, build)
+        self._finish_swap(n_new, len(self.active_doc_lens) - bp.keep_docs,
+                          new_lens[bp.first_new:bp.first_new + bp.new_docs])
 
     def state_dict(self) -> dict:
         """Corpus, suffix array, delta and document lengths as host tensors
@@ -516,8 +465,9 @@ class GlobalIndex:
         self.delta_len = int(delta.numel())
         self.delta_len_t.fill_(self.delta_len)
         self.active_len = n
-        self.active_doc_lens = deque(int(x) for x in state["active_doc_lens"])
-        self.delta_doc_lens = [int(x) for x in state["delta_doc_lens"]]
+        self.active_doc_lens = DocLedger(int(x)
+                                         for x in state["active_doc_lens"])
+        self.delta_doc_lens = DocLedger(int(x) for x in state["delta_doc_lens"])
         r = state.get("sa_rounds")
         self._sa_rounds = None if r is None else int(r)
 

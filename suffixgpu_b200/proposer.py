@@ -87,6 +87,27 @@ class SuffixGPUDrafter:
                 rebuild_stream=rebuild_stream)
 
     # ------------------------------------------------------------------
+    def device_error(self, clear: bool = True,
+                     raise_on_error: bool = False) -> int:
+        """Bits of the device error word (SG_DEVERR_WAIT = 1: a row's load
+        into the local kernel's shared memory did not land within the
+        kernel's bounded wait, and that row drafted nothing); 0 when no
+        kernel has failed. Clears the word by default. Synchronises the
+        current stream, so call it off the decode loop's hot path (a
+        periodic health check). No reference counterpart: the reference's
+        kernels have no bounded waits."""
+        from suffixgpu_b200._lib import check, lib, stream_of
+        import ctypes
+        bits = ctypes.c_uint32(0)
+        check("sg_device_error", lib().sg_device_error(
+            ctypes.byref(bits), int(clear), stream_of(self.device)))
+        if bits.value and raise_on_error:
+            raise RuntimeError(
+                f"device error word {bits.value:#x}: a bounded wait of the "
+                "local draft kernel ran out; the affected rows drafted "
+                "nothing")
+        return bits.value
+
     def poll(self) -> None:
         """Host-side: swap in a finished background rebuild, if any."""
         if self.global_index is not None:
@@ -216,8 +237,18 @@ class SuffixGPUDrafter:
     # ------------------------------------------------------------------
     def harvest_finished(self, row_indices: list[int], lengths: list[int],
                          token_ids_gpu: torch.Tensor) -> None:
-        rows = [token_ids_gpu[r] for r in row_indices]
-        self.harvest_rows(rows, lengths)
+        """Rows' first ``lengths`` tokens become documents of the global
+        index (proposer.py:329-343)."""
+        if self.global_index is None:
+            return
+        self._append_rows(token_ids_gpu, list(row_indices), list(lengths))
+
+    def _append_rows(self, token_ids: torch.Tensor, rows: list[int],
+                     lengths: list[int]) -> None:
+        """harvest_finished's documents, written straight from the token
+        buffer (one launch). The multi-GPU drafter exchanges them between
+        ranks here."""
+        self.global_index.append_rows(token_ids, rows, lengths)
 
     def harvest_rows(self, rows: list[torch.Tensor],
                      lengths: list[int]) -> None:

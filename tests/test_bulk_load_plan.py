@@ -9,23 +9,17 @@ import numpy as np
 import pytest
 
 from oracle import suffix_oracle as so
-from suffixgpu_b200.global_index import plan_bulk_load
+from suffixgpu_b200.doc_ledger import plan_bulk_load
 
 
 def _final_docs(active_docs, new_docs, capacity):
     """The product's plan applied to host document lists."""
     a_lens = [d.size + 1 for d in active_docs]
     n_lens = [d.size + 1 for d in new_docs]
-    keep, first, count, _ = plan_bulk_load(a_lens, sum(a_lens), n_lens,
-                                           capacity)
-    kept = []
-    acc = 0
-    for d in reversed(active_docs):
-        if acc >= keep:
-            break
-        kept.append(d)
-        acc += d.size + 1
-    return list(reversed(kept)) + new_docs[first:first + count]
+    bp = plan_bulk_load(a_lens, n_lens, capacity)
+    kept = active_docs[len(active_docs) - bp.keep_docs:]
+    assert sum(d.size + 1 for d in kept) == bp.keep_tokens
+    return kept + new_docs[bp.first_new:bp.first_new + bp.new_docs]
 
 
 def _corpus(docs):

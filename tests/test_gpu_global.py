@@ -487,7 +487,7 @@ def test_state_dict_round_trip():
         assert torch.equal(getattr(g, name), getattr(h, name)), name
     assert torch.equal(g.delta[:g.delta_len], h.delta[:h.delta_len])
     assert list(g.active_doc_lens) == list(h.active_doc_lens)
-    assert g.delta_doc_lens == h.delta_doc_lens
+    assert list(g.delta_doc_lens) == list(h.delta_doc_lens)
     q = _dev(rng.integers(0, 7, size=(16, 9)).astype(np.int32))
     qlen = _dev(rng.integers(0, 10, size=16).astype(np.int64))
     for a, b in zip(g.query(q, qlen, 8), h.query(q, qlen, 8)):

@@ -7,7 +7,10 @@ from a scratch array compiled into the library. These tests call it through
 the C ABI, twice in a row with different inputs (the second call reuses the
 scratch the first one left behind), and require the same suffix arrays and
 round counts as sg_build_suffix_array with a caller-allocated workspace.
-Inputs and outputs are allocated by the test, as the caller would.
+Inputs and outputs are allocated by the test, as the caller would. The
+largest accepted input is checked against the numpy oracle's suffix array
+(suffix_gpu/suffix_array.py:15-63 restated), and the size limit is checked
+at its exact boundary.
 """
 
 from __future__ import annotations
@@ -71,6 +74,40 @@ def test_noalloc_matches_workspace_build_twice_in_a_row():
         exp, exp_rounds = _build_with_workspace(lib, tok)
         np.testing.assert_array_equal(got, exp)
         assert rounds == exp_rounds
+
+
+def _max_tokens(lib) -> int:
+    """Largest n whose build workspace fits the 8 MiB scratch array."""
+    lo, hi = 0, 1 << 23
+    while lo < hi:
+        mid = (lo + hi + 1) // 2
+        if lib.sg_suffix_array_workspace_size(mid) <= 8 << 20:
+            lo = mid
+        else:
+            hi = mid - 1
+    return lo
+
+
+def test_noalloc_at_its_limit_matches_the_oracle():
+    """The largest accepted n builds the oracle's suffix array; n + 1 is
+    refused before any launch."""
+    from oracle import suffix_oracle as so
+    lib = _lib()
+    n = _max_tokens(lib)
+    assert 150_000 < n < 160_000
+    tok = _tokens(3, n + 1, 3000)
+    out = torch.full((n + 1,), -7, dtype=torch.int32, device=tok.device)
+    rounds = ctypes.c_int32(0)
+    st = lib.sg_build_suffix_array_noalloc(
+        tok.data_ptr(), n + 1, out.data_ptr(), ctypes.byref(rounds),
+        torch.cuda.current_stream().cuda_stream)
+    assert st == 4  # SG_ERR_UNSUPPORTED
+    torch.cuda.synchronize()
+    assert (out == -7).all()  # nothing was launched
+    _build_noalloc(lib, tok[:n], out[:n])
+    torch.cuda.synchronize()
+    exp = so.build_suffix_array(tok[:n].cpu().numpy())
+    np.testing.assert_array_equal(out[:n].cpu().numpy(), exp)
 
 
 def test_noalloc_rejects_inputs_beyond_its_scratch():
