@@ -409,6 +409,81 @@ int sg_global_draft(const int64_t* sa_len, const int64_t* sa_start,
                     const float* local_score, const uint8_t* row_mask,
                     int32_t* draft, int32_t* num_valid, sg_stream_t stream);
 
+/* ---- suffix-array shards (multi-GPU global drafter) ---
+ * No reference counterpart: the reference has one suffix array on one
+ * device. These calls split its query across GPUs without changing its
+ * result: each GPU keeps the suffixes that start in its share of the corpus
+ * (in suffix-array order, each with its global rank), searches every row
+ * of the job on them, and the per-GPU results are summed by collectives
+ * (see suffixgpu_b200/distributed.py). The reference behaviour reproduced
+ * is suffix_match_backoff (sa_search.py:110-163) and the strided sample of
+ * _query_backoff (global_index.py:339-352). */
+
+/* Workspace bytes of sg_shard_extract for an n-entry suffix array. */
+size_t sg_shard_extract_workspace_size(int64_t n);
+
+/* The shard [lo, hi) of a whole-corpus suffix array sa[0..n): shard_pos[k]
+ * = the k-th entry of sa whose position lies in [lo, hi) (sa order, so the
+ * shard's own suffix array) and shard_rank[k] = its index in sa (its global
+ * rank). Both outputs hold hi - lo entries (every position occurs once). */
+int sg_shard_extract(const int32_t* sa, int64_t n, int64_t lo, int64_t hi,
+                     int32_t* shard_pos, int32_t* shard_rank, void* workspace,
+                     size_t workspace_bytes, sg_stream_t stream);
+
+/* Packed query rows [batch, max_len + 2] int32: the tail (max_len tokens,
+ * oldest first, sg_gather_tails' layout), the tail length and the drafting
+ * flag (row_mask[b] != 0; all rows when row_mask is NULL). */
+int sg_shard_pack_rows(const int32_t* tails, const int64_t* tail_len,
+                       const uint8_t* row_mask, int32_t batch,
+                       int32_t max_len, int32_t* rows, sg_stream_t stream);
+
+/* Per packed row b and length l = 1..max_len: out_bounds[b, l-1, 0..1] =
+ * (lower, upper) of the tail's last l tokens over the shard's suffix array
+ * shard_sa[0..shard_n) (positions into corpus[0..corpus_n)): the number of
+ * shard suffixes below the pattern and the number not above it, i.e. the
+ * search_interval bounds on that array (sa_search.py:66-107, comparator
+ * :25-63 with the whole corpus's end). Zeros for rows that do not draft and
+ * lengths beyond the tail. Summed over all shards of a corpus they equal
+ * search_interval on the whole suffix array. max_len <= 128. */
+int sg_shard_bounds(const int32_t* shard_sa, int64_t shard_n,
+                    const int32_t* corpus, int64_t corpus_n,
+                    const int32_t* rows, int32_t batch, int32_t max_len,
+                    int32_t* out_bounds, sg_stream_t stream);
+
+/* From the summed bounds (bounds_sum, every shard's sg_shard_bounds added)
+ * and this shard's own (bounds_local), per row and cap: the best length
+ * (the longest <= cap and <= the tail length with a non-empty interval),
+ * and samples[b, c, j] for j < R = the corpus position of sample j of that
+ * interval (start + floor(j * ilen / R) when ilen > R, else start + j,
+ * global ranks) when this shard holds it, else 0. Caps whose best length
+ * equals the previous cap's get zeros (they share its samples). For rows
+ * own_lo .. own_lo + own_n - 1, sa_len / sa_start / sa_end [own_n, C]
+ * int64 receive sg_global_draft_samples' per-cap inputs: the best length
+ * and the [start, end) slice of the samples array ([own_n, C, R] laid out
+ * like samples' rows own_lo..) holding its min(ilen, R) samples in order.
+ * num_caps <= 16. */
+int sg_shard_resolve(const int32_t* bounds_sum, const int32_t* bounds_local,
+                     const int32_t* rows, int32_t batch, int32_t max_len,
+                     const int64_t* caps, int32_t num_caps, int32_t max_occ,
+                     const int32_t* shard_pos, const int32_t* shard_rank,
+                     int32_t* samples, int32_t own_lo, int32_t own_n,
+                     int64_t* sa_len, int64_t* sa_start, int64_t* sa_end,
+                     sg_stream_t stream);
+
+/* sg_global_draft with the suffix array replaced by a block of resolved
+ * samples (num_samples int32 corpus positions, indexed by sample_start /
+ * sample_end from sg_shard_resolve). Same outputs and limits. */
+int sg_global_draft_samples(
+    const int64_t* sa_len, const int64_t* sample_start,
+    const int64_t* sample_end, const int64_t* d_len, const int64_t* d_pos,
+    const int64_t* d_cnt, const int32_t* samples, int64_t num_samples,
+    const int32_t* corpus, int64_t capacity, const int32_t* delta,
+    int64_t delta_capacity, const int64_t* delta_len, int32_t batch,
+    int32_t num_caps, int32_t max_occ, int32_t k, int32_t has_spec_factor,
+    float spec_factor, float spec_offset, float min_token_prob, float alpha,
+    const float* local_score, const uint8_t* row_mask, int32_t* draft,
+    int32_t* num_valid, sg_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

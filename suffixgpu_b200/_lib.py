@@ -110,6 +110,23 @@ _SIGS: dict[str, list] = {
     "sg_delta_compact": [c_void_p, c_int64, c_int64, c_int64, c_void_p,
                          c_void_p],
     "sg_device_error": [POINTER(ctypes.c_uint32), c_int, c_void_p],
+    "sg_shard_extract": [c_void_p, c_int64, c_int64, c_int64, c_void_p,
+                         c_void_p, c_void_p, c_size_t, c_void_p],
+    "sg_shard_pack_rows": [c_void_p, c_void_p, c_void_p, c_int32, c_int32,
+                           c_void_p, c_void_p],
+    "sg_shard_bounds": [c_void_p, c_int64, c_void_p, c_int64, c_void_p,
+                        c_int32, c_int32, c_void_p, c_void_p],
+    "sg_shard_resolve": [c_void_p, c_void_p, c_void_p, c_int32, c_int32,
+                         c_void_p, c_int32, c_int32, c_void_p, c_void_p,
+                         c_void_p, c_int32, c_int32, c_void_p, c_void_p,
+                         c_void_p, c_void_p],
+    "sg_global_draft_samples": [c_void_p, c_void_p, c_void_p, c_void_p,
+                                c_void_p, c_void_p, c_void_p, c_int64,
+                                c_void_p, c_int64, c_void_p, c_int64,
+                                c_void_p, c_int32, c_int32, c_int32, c_int32,
+                                c_int32, c_float, c_float, c_float, c_float,
+                                c_void_p, c_void_p, c_void_p, c_void_p,
+                                c_void_p],
     "sg_global_combine": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                           c_void_p, c_void_p, c_int32, c_int32, c_int32,
                           c_void_p],
@@ -151,6 +168,7 @@ _SIGS_EXTRA: dict[str, tuple] = {
     "sg_suffix_array_workspace_size": (c_size_t, [c_int64]),
     "sg_set_wait_polls": (c_int, [c_int]),
     "sg_suffix_array_append_workspace_size": (c_size_t, [c_int64]),
+    "sg_shard_extract_workspace_size": (c_size_t, [c_int64]),
 }
 
 

@@ -116,6 +116,7 @@ struct GlobalCandArgs {
   const int32_t* sa;
   const int32_t* corpus;
   int64_t capacity;
+  int64_t sa_entries;  // entries of sa (capacity, or a sample block's size)
   const int32_t* delta;
   int64_t delta_capacity;
   const int64_t* delta_len;  // device scalar
@@ -213,7 +214,7 @@ __device__ __forceinline__ long long occ_key(const GlobalCandArgs& a,
     const long long ilen = pl.ilen[c], st = pl.start[c];
     long long idx = ilen > a.R ? st + (static_cast<long long>(r) * ilen) / a.R
                                : st + r;
-    idx = idx < 0 ? 0 : (idx > a.capacity - 1 ? a.capacity - 1 : idx);
+    idx = idx < 0 ? 0 : (idx > a.sa_entries - 1 ? a.sa_entries - 1 : idx);
     return a.sa[idx];
   }
   return a.d_pos[o * a.R + r];
@@ -532,7 +533,8 @@ extern "C" int sg_global_candidates(
       !corpus || !delta || !delta_len || !match_len || !cont || !occ_count)
     return SG_ERR_INVALID;
   GlobalCandArgs a{sa_len, sa_start, sa_end, d_len, d_pos, d_cnt, sa,
-                   corpus, capacity, delta, delta_capacity, delta_len,
+                   corpus, capacity, capacity, delta, delta_capacity,
+                   delta_len,
                    batch, num_caps, max_occ, k, has_spec_factor,
                    spec_factor, spec_offset, match_len, cont, occ_count,
                    spec_cap};
@@ -559,19 +561,18 @@ extern "C" int sg_global_combine(int32_t* draft, int32_t* num_valid,
   return check_launch();
 }
 
-extern "C" int sg_global_draft(
+static int global_draft_impl(
     const int64_t* sa_len, const int64_t* sa_start, const int64_t* sa_end,
     const int64_t* d_len, const int64_t* d_pos, const int64_t* d_cnt,
-    const int32_t* sa, const int32_t* corpus, int64_t capacity,
-    const int32_t* delta, int64_t delta_capacity, const int64_t* delta_len,
-    int32_t batch, int32_t num_caps, int32_t max_occ, int32_t k,
-    int32_t has_spec_factor, float spec_factor, float spec_offset,
-    float min_token_prob, float alpha, const float* local_score,
-    const uint8_t* row_mask, int32_t* draft, int32_t* num_valid,
-    sg_stream_t stream) {
-  sg::NvtxScope nvtx_range("sg_global_draft");
+    const int32_t* sa, int64_t sa_entries, const int32_t* corpus,
+    int64_t capacity, const int32_t* delta, int64_t delta_capacity,
+    const int64_t* delta_len, int32_t batch, int32_t num_caps,
+    int32_t max_occ, int32_t k, int32_t has_spec_factor, float spec_factor,
+    float spec_offset, float min_token_prob, float alpha,
+    const float* local_score, const uint8_t* row_mask, int32_t* draft,
+    int32_t* num_valid, sg_stream_t stream) {
   if (batch < 0 || num_caps < 1 || num_caps > kGMaxCaps || max_occ < 1 ||
-      max_occ > 1024 || k < 1 || k > 64 || capacity < 1 ||
+      max_occ > 1024 || k < 1 || k > 64 || capacity < 1 || sa_entries < 1 ||
       delta_capacity < 1)
     return SG_ERR_INVALID;
   if (batch == 0) return SG_OK;
@@ -583,10 +584,10 @@ extern "C" int sg_global_draft(
     return SG_ERR_UNSUPPORTED;
   GlobalDraftArgs d;
   d.g = GlobalCandArgs{sa_len, sa_start, sa_end, d_len, d_pos, d_cnt, sa,
-                       corpus, capacity, delta, delta_capacity, delta_len,
-                       batch, num_caps, max_occ, k, has_spec_factor,
-                       spec_factor, spec_offset, nullptr, nullptr, nullptr,
-                       nullptr};
+                       corpus, capacity, sa_entries, delta, delta_capacity,
+                       delta_len, batch, num_caps, max_occ, k,
+                       has_spec_factor, spec_factor, spec_offset, nullptr,
+                       nullptr, nullptr, nullptr};
   d.min_prob = min_token_prob;
   d.alpha = alpha;
   d.draft = draft;
@@ -597,4 +598,42 @@ extern "C" int sg_global_draft(
   if (max_occ <= 128) return launch_global_draft<4>(d, st);
   if (max_occ <= 256) return launch_global_draft<8>(d, st);
   return launch_global_draft<32>(d, st);
+}
+
+extern "C" int sg_global_draft(
+    const int64_t* sa_len, const int64_t* sa_start, const int64_t* sa_end,
+    const int64_t* d_len, const int64_t* d_pos, const int64_t* d_cnt,
+    const int32_t* sa, const int32_t* corpus, int64_t capacity,
+    const int32_t* delta, int64_t delta_capacity, const int64_t* delta_len,
+    int32_t batch, int32_t num_caps, int32_t max_occ, int32_t k,
+    int32_t has_spec_factor, float spec_factor, float spec_offset,
+    float min_token_prob, float alpha, const float* local_score,
+    const uint8_t* row_mask, int32_t* draft, int32_t* num_valid,
+    sg_stream_t stream) {
+  sg::NvtxScope nvtx_range("sg_global_draft");
+  return global_draft_impl(sa_len, sa_start, sa_end, d_len, d_pos, d_cnt, sa,
+                           capacity, corpus, capacity, delta, delta_capacity,
+                           delta_len, batch, num_caps, max_occ, k,
+                           has_spec_factor, spec_factor, spec_offset,
+                           min_token_prob, alpha, local_score, row_mask,
+                           draft, num_valid, stream);
+}
+
+extern "C" int sg_global_draft_samples(
+    const int64_t* sa_len, const int64_t* sample_start,
+    const int64_t* sample_end, const int64_t* d_len, const int64_t* d_pos,
+    const int64_t* d_cnt, const int32_t* samples, int64_t num_samples,
+    const int32_t* corpus, int64_t capacity, const int32_t* delta,
+    int64_t delta_capacity, const int64_t* delta_len, int32_t batch,
+    int32_t num_caps, int32_t max_occ, int32_t k, int32_t has_spec_factor,
+    float spec_factor, float spec_offset, float min_token_prob, float alpha,
+    const float* local_score, const uint8_t* row_mask, int32_t* draft,
+    int32_t* num_valid, sg_stream_t stream) {
+  sg::NvtxScope nvtx_range("sg_global_draft_samples");
+  return global_draft_impl(sa_len, sample_start, sample_end, d_len, d_pos,
+                           d_cnt, samples, num_samples, corpus, capacity,
+                           delta, delta_capacity, delta_len, batch, num_caps,
+                           max_occ, k, has_spec_factor, spec_factor,
+                           spec_offset, min_token_prob, alpha, local_score,
+                           row_mask, draft, num_valid, stream);
 }

@@ -234,11 +234,13 @@ __device__ __forceinline__ uint32_t sa_mid(uint32_t lo, uint32_t hi,
 // the upper bound above it, both probes of a step loaded together. Once a
 // bound's range is empty every further step of the reference's fixed
 // ceil(log2(n + 1)) count leaves it unchanged, so its loop stops there.
+// n: entries of sa; nc: tokens of corpus (equal for a whole-corpus suffix
+// array; a shard's suffix array holds fewer entries than the corpus).
 template <int NC>
 __device__ __forceinline__ void warp_bounds_cols(
     const int32_t* __restrict__ sa, const int32_t* __restrict__ corpus,
-    uint32_t n, int iters, const int (&pc)[NC], int M, int lim, int64_t plen,
-    uint32_t& out_lo, uint32_t& out_hi) {
+    uint32_t n, uint32_t nc, int iters, const int (&pc)[NC], int M, int lim,
+    int64_t plen, uint32_t& out_lo, uint32_t& out_hi) {
   uint32_t lo = 0, hi = n;
   int it = 0;
   uint32_t eq = 0;
@@ -246,7 +248,7 @@ __device__ __forceinline__ void warp_bounds_cols(
   for (; it < iters && lo < hi; ++it) {
     const uint32_t mid = sa_mid(lo, hi, n);
     int tok[NC], tm;
-    load_probe<NC>(corpus, n, static_cast<uint32_t>(sa[mid]), lim, plen, M,
+    load_probe<NC>(corpus, nc, static_cast<uint32_t>(sa[mid]), lim, plen, M,
                    tok, tm);
     const int c = cmp_probe<NC>(tok, tm, pc, lim, plen, M);
     if (c < 0) {
@@ -270,9 +272,9 @@ __device__ __forceinline__ void warp_bounds_cols(
     const uint32_t ml = sa_mid(llo, lhi, n), mu = sa_mid(ulo, uhi, n);
     // (a finished bound loads nothing: zero columns, no column M)
     int tl[NC], tml, tu[NC], tmu;
-    load_probe<NC>(corpus, n, static_cast<uint32_t>(sa[ml]), dl ? lim : 0,
+    load_probe<NC>(corpus, nc, static_cast<uint32_t>(sa[ml]), dl ? lim : 0,
                    dl ? plen : 0, M, tl, tml);
-    load_probe<NC>(corpus, n, static_cast<uint32_t>(sa[mu]), du ? lim : 0,
+    load_probe<NC>(corpus, nc, static_cast<uint32_t>(sa[mu]), du ? lim : 0,
                    du ? plen : 0, M, tu, tmu);
     if (dl) {
       if (cmp_probe<NC>(tl, tml, pc, lim, plen, M) < 0)
@@ -297,15 +299,16 @@ template <int NC>
 __device__ __forceinline__ void warp_bounds(
     const int32_t* __restrict__ sa, const int32_t* __restrict__ corpus,
     int64_t n, int iters, const int (&pc)[NC], int M, int64_t plen,
-    int64_t& lower, int64_t& upper) {
+    int64_t& lower, int64_t& upper, int64_t nc = -1) {
   const int lim = plen < M ? (plen > 0 ? static_cast<int>(plen) : 0) : M;
   const uint32_t un = static_cast<uint32_t>(n);
+  const uint32_t unc = static_cast<uint32_t>(nc < 0 ? n : nc);
   uint32_t a, b;
   if (NC > 1 && lim <= 32 && plen <= M) {
     const int pc1[1] = {pc[0]};
-    warp_bounds_cols<1>(sa, corpus, un, iters, pc1, M, lim, plen, a, b);
+    warp_bounds_cols<1>(sa, corpus, un, unc, iters, pc1, M, lim, plen, a, b);
   } else {
-    warp_bounds_cols<NC>(sa, corpus, un, iters, pc, M, lim, plen, a, b);
+    warp_bounds_cols<NC>(sa, corpus, un, unc, iters, pc, M, lim, plen, a, b);
   }
   lower = a;
   upper = b;
@@ -403,6 +406,44 @@ __global__ void __cluster_dims__(kSCG, 1, 1) __launch_bounds__(512)
       out_start[o] = best > 0 ? s_all[2 * best - 2] : 0;
       out_end[o] = best > 0 ? s_all[2 * best - 1] : 0;
     }
+  }
+}
+
+// Shard search: every (row, length) interval of the rows' tails over one
+// shard's suffix array (the whole-corpus suffix array restricted to the
+// suffixes that start in the shard, in the same order). One warp per
+// (row, length); rows are packed as [tail (M tokens, oldest first), tail
+// length, drafting flag] int32. The bounds count the shard's suffixes
+// below the pattern (lower) and not above it (upper), so summing them over
+// all shards gives the whole-corpus interval.
+template <int NC>
+__global__ void __launch_bounds__(kSWarps * 32)
+    shard_bounds_kernel(const int32_t* __restrict__ sa, int64_t ns,
+                        const int32_t* __restrict__ corpus, int64_t nc,
+                        const int32_t* __restrict__ rows, int B, int W, int M,
+                        int iters, int32_t* __restrict__ out) {
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * kSWarps + warp_id();
+  if (w >= static_cast<int64_t>(B) * M) return;  // warp-uniform
+  const int b = static_cast<int>(w / M), l = static_cast<int>(w % M) + 1;
+  const int lane = lane_id();
+  const int32_t* row = rows + static_cast<int64_t>(b) * W;
+  const int tl = row[M], active = row[M + 1];
+  int64_t lo = 0, hi = 0;
+  if (active && l <= tl && ns > 0) {
+    int pc[NC];
+    const int o = tl - l;
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+      const int j = lane + 32 * k;
+      const int x = o + j;
+      pc[k] = j < l ? row[x < M ? x : M - 1] : 0;
+    }
+    warp_bounds<NC>(sa, corpus, ns, sa_iters(ns), pc, M, l, lo, hi, nc);
+  }
+  (void)iters;
+  if (lane == 0) {
+    out[2 * w] = static_cast<int32_t>(lo);
+    out[2 * w + 1] = static_cast<int32_t>(hi);
   }
 }
 
@@ -510,5 +551,38 @@ extern "C" int sg_suffix_match_backoff(
                       reinterpret_cast<cudaStream_t>(stream)>>>(
       sa, corpus, n, query, query_width, query_len, max_len, caps, num_caps,
       row_mask, sa_iters(n), out_len, out_start, out_end);
+  return check_launch();
+}
+
+extern "C" int sg_shard_bounds(const int32_t* shard_sa, int64_t shard_n,
+                               const int32_t* corpus, int64_t corpus_n,
+                               const int32_t* rows, int32_t batch,
+                               int32_t max_len, int32_t* out_bounds,
+                               sg_stream_t stream) {
+  sg::NvtxScope nvtx_range("sg_shard_bounds");
+  if (shard_n < 0 || corpus_n < 1 || corpus_n > INT32_MAX ||
+      shard_n > corpus_n || batch < 0 || max_len < 1 ||
+      max_len > 32 * kSMaxCols)
+    return SG_ERR_INVALID;
+  if (batch == 0) return SG_OK;
+  if ((shard_n > 0 && !shard_sa) || !corpus || !rows || !out_bounds)
+    return SG_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t warps = static_cast<int64_t>(batch) * max_len;
+  const unsigned blocks = static_cast<unsigned>((warps + kSWarps - 1) / kSWarps);
+  const int W = max_len + 2;
+  const int it = sa_iters(shard_n > 0 ? shard_n : 1);
+  if (max_len <= 32)
+    shard_bounds_kernel<1><<<blocks, kSWarps * 32, 0, st>>>(
+        shard_sa, shard_n, corpus, corpus_n, rows, batch, W, max_len, it,
+        out_bounds);
+  else if (max_len <= 64)
+    shard_bounds_kernel<2><<<blocks, kSWarps * 32, 0, st>>>(
+        shard_sa, shard_n, corpus, corpus_n, rows, batch, W, max_len, it,
+        out_bounds);
+  else
+    shard_bounds_kernel<4><<<blocks, kSWarps * 32, 0, st>>>(
+        shard_sa, shard_n, corpus, corpus_n, rows, batch, W, max_len, it,
+        out_bounds);
   return check_launch();
 }

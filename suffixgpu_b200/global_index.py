@@ -28,6 +28,8 @@ import queue
 import threading
 import time
 import weakref
+from collections import deque
+
 import torch
 
 from suffixgpu_b200 import ops
@@ -145,6 +147,9 @@ class GlobalIndex:
         # Multi-GPU: maps "my rebuild has finished" to "every rank's has",
         # so that replicas of the index swap at the same call.
         self.rebuild_agree = None
+        # callables run after a new suffix array became the active one
+        # (suffix-array shards re-extract theirs)
+        self.on_swap: list = []
 
     # ------------------------------------------------------------------
     # writes (global_index.py:86-133)
@@ -370,6 +375,8 @@ class GlobalIndex:
         self._rebuild_event = None
         self._pending = None
         self.rebuilds += 1
+        for fn in self.on_swap:
+            fn()
 
     def poll_rebuild(self) -> None:
         """Swap in a finished background rebuild (non-blocking)."""
@@ -470,6 +477,8 @@ class GlobalIndex:
         self.delta_doc_lens = DocLedger(int(x) for x in state["delta_doc_lens"])
         r = state.get("sa_rounds")
         self._sa_rounds = None if r is None else int(r)
+        for fn in self.on_swap:
+            fn()
 
     def wait_rebuild(self) -> None:
         """Block until an in-flight background rebuild has finished and

@@ -1,7 +1,7 @@
 """Multi-rank host logic of the multi-GPU drafter on CPU: two gloo ranks
 (spawned processes, 127.0.0.1) exchange harvested documents and agree on
 rebuild swaps. The per-rank index here is the oracle's, fed exactly as the
-product's ShardedSuffixDrafter feeds its GlobalIndex, so the test shows the
+product's multi-GPU drafters feed their GlobalIndex, so the test shows the
 replicas stay identical to one index that receives all ranks' documents in
 rank order."""
 

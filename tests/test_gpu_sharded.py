@@ -1,8 +1,9 @@
-"""The multi-GPU drafter on GPUs: with one rank it is the plain drafter;
-with two ranks (NCCL, one process per GPU; skipped on one-GPU machines)
-each rank's drafts equal those of one drafter that drafts all rows and
-receives every rank's harvested documents in rank order, and replicas
-with background rebuilds stay identical."""
+"""The multi-GPU drafters on GPUs. The replicated-index drafter: with one
+rank it is the plain drafter; with two ranks (NCCL, one process per GPU;
+skipped on one-GPU machines) each rank's drafts equal those of one drafter
+that drafts all rows and receives every rank's harvested documents in rank
+order, and replicas with background rebuilds stay identical. The sharded
+suffix-array drafter: tested in test_gpu_sa_shards.py."""
 
 from __future__ import annotations
 
@@ -75,10 +76,10 @@ def _single_reference(sc):
     return out
 
 
-def test_sharded_world_one_matches_drafter():
+def test_replicated_world_one_matches_drafter():
     import torch.distributed as dist
     from suffixgpu_b200 import SuffixGPUDrafter
-    from suffixgpu_b200.distributed import ShardedSuffixDrafter
+    from suffixgpu_b200.distributed import ReplicatedSuffixDrafter
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(_free_port())
     dist.init_process_group("nccl", rank=0, world_size=1)
@@ -88,7 +89,7 @@ def test_sharded_world_one_matches_drafter():
         b = sc["data"]["token_ids"].shape[0]
         rows = list(range(b))
         dev = torch.device("cuda")
-        got, _ = _run(sc, ShardedSuffixDrafter(device=dev, **sc["drafter"]),
+        got, _ = _run(sc, ReplicatedSuffixDrafter(device=dev, **sc["drafter"]),
                       rows, 1, 0, dev)
         exp, _ = _run(sc, SuffixGPUDrafter(device=dev, **sc["drafter"]),
                       rows, 1, 0, dev)
@@ -101,7 +102,7 @@ def test_sharded_world_one_matches_drafter():
 
 def _two_rank_worker(rank, port, sc, q):
     import torch.distributed as dist
-    from suffixgpu_b200.distributed import ShardedSuffixDrafter
+    from suffixgpu_b200.distributed import ReplicatedSuffixDrafter
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
@@ -110,9 +111,9 @@ def _two_rank_worker(rank, port, sc, q):
         dev = torch.device("cuda", rank)
         b = sc["data"]["token_ids"].shape[0]
         rows = list(range(rank * b // 2, (rank + 1) * b // 2))
-        d = ShardedSuffixDrafter(device=dev, **sc["drafter"])
+        d = ReplicatedSuffixDrafter(device=dev, **sc["drafter"])
         sync_out, _ = _run(sc, d, rows, 2, rank, dev)
-        d2 = ShardedSuffixDrafter(device=dev,
+        d2 = ReplicatedSuffixDrafter(device=dev,
                                   rebuild_stream=torch.cuda.Stream(dev),
                                   **sc["drafter"])
         _, sums = _run(sc, d2, rows, 2, rank, dev)
@@ -122,7 +123,7 @@ def _two_rank_worker(rank, port, sc, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_sharded_two_gpus_match_single_index():
+def test_replicated_two_gpus_match_single_index():
     import torch.multiprocessing as mp
     sc = scenarios.global_scenario(44, steps=12)
     ctx = mp.get_context("spawn")

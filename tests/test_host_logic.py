@@ -44,6 +44,7 @@ def _bare_index(doc_lens):
     gi._rebuild_event = object()
     gi._pending = object()
     gi.rebuilds = 0
+    gi.on_swap = []
     return gi
 
 

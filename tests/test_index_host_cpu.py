@@ -100,6 +100,7 @@ def host_index(monkeypatch):
         gi.last_build = None
         gi.build_log = deque(maxlen=16)
         gi.rebuild_agree = None
+        gi.on_swap = []
         return gi
     return make
 
