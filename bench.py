@@ -283,18 +283,34 @@ def run_ours(args):
             _, _, cur[r] = drafter.propose_with_update(
                 cur[r], rp["tok"], rp["samp"][j])
 
-    def capture(seq):
+    def capture(seq, marks=None):
+        """A graph of the steps; with marks = (start, end) events, their
+        records are the graph's first and last nodes."""
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
+            if marks:
+                marks[0].record()
             run_seq(seq)
+            if marks:
+                marks[1].record()
         return g
 
     # warm-up: eager calls (exercise the API), then the graphs once
     run_seq(step_seq(max(args.warmup, 3)))
     torch.cuda.synchronize()
-    full = capture(step_seq(cycle)) if args.steps >= cycle else None
-    rem = args.steps % cycle
-    part = capture(step_seq(rem)) if rem else None
+    # Up to one decode cycle the timed steps are one graph whose first and
+    # last nodes record the timing events, so the window holds exactly the
+    # K steps on the device (no graph launch latency); longer runs replay
+    # cycle graphs inside a busy-stream window.
+    marks = None
+    if args.steps <= cycle:
+        marks = tuple(torch.cuda.Event(enable_timing=True, external=True)
+                      for _ in range(2))
+        full, part = None, capture(step_seq(args.steps), marks)
+    else:
+        full = capture(step_seq(cycle))
+        rem = args.steps % cycle
+        part = capture(step_seq(rem)) if rem else None
     for g in (full, part):
         if g is not None:
             g.replay()
@@ -313,6 +329,10 @@ def run_ours(args):
             part.replay()
 
     ms = device_window(replays, world)
+    timing = "busy-stream window around the graph replays"
+    if marks is not None:
+        ms = marks[0].elapsed_time(marks[1])
+        timing = "events recorded by the timed graph's first and last nodes"
     clocks = clock.stop()
     ms_ranks = ranks_ms(ms, world, dev)
     ms_max = max(ms_ranks)
@@ -346,7 +366,8 @@ def run_ours(args):
             "vs_baseline": None,
             "dtype": "int32",
             "data": "synthetic (seeded copy/Zipf rows, BASELINE config 2)",
-            "config": dict(CONFIG, parallelism=f"dp{world}"),
+            "config": dict(CONFIG, parallelism=f"dp{world}",
+                           timing=timing),
             "impl": "ours",
             "gpu_launches": launches,
             "e2e": e2e,
@@ -552,31 +573,52 @@ def run_sharded(args, dev, world: int, rank: int) -> dict | None:
     query rows (S=16384) per GPU, k=32, P=64, R=256, 8 backoff levels,
     factor 2.0, min_prob 0.1, over a 2^26-token template corpus (512
     templates x 512, vocab 128256) that every rank bulk-loads from the same
-    seed (ShardedSuffixDrafter: replicated index, rows per rank; the plain
-    drafter on one GPU). One step = one propose_with_update of the rank's
-    rows; steps replay from a CUDA graph over 16 rotating replicas of the
-    token buffer (128 MiB > L2), each walking a 32-step decode loop. Value:
-    all ranks' rows / max-over-ranks time (weak scaling)."""
+    seed. Two multi-GPU modes, both bit-exact to one index:
+    ``shards`` (config 5 as specified: each rank queries its 2^26 / N
+    positions' part of the suffix array, three collectives per step) and
+    ``replicated`` (the whole suffix array on every rank, no collective).
+    One step = one propose_with_update of the rank's rows over 16 rotating
+    replicas of the token buffer (128 MiB > L2), each walking a 32-step
+    decode loop; steps are replayed from a CUDA graph when capture works
+    (eager otherwise). Value: all ranks' rows / max-over-ranks device time
+    (weak scaling). The shards mode also reports per-phase device times of
+    a few eager steps (rank 0 and the max over ranks)."""
     import torch
-    import torch.distributed as dist
-    from suffixgpu_b200 import SuffixGPUDrafter
     from suffixgpu_b200 import workloads as wl
     lg = min(26, max(16, args.sharded_log2_corpus))
     data = wl.config5(rank=rank, steps=DECODE5, n_docs=1 << (lg - 10))
+    docs = torch.from_numpy(data["corpus_docs"]).to(dev)
+    res = {}
+    for mode in ("shards", "replicated"):
+        res[mode] = _run_config5_mode(args, dev, world, rank, mode, data,
+                                      docs, lg)
+        torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    out = res["shards"]
+    out["replicated"] = res["replicated"]
+    return out
+
+
+def _run_config5_mode(args, dev, world, rank, mode, data, docs, lg):
+    import torch
+    from suffixgpu_b200 import SuffixGPUDrafter
+    from suffixgpu_b200 import workloads as wl
+    from suffixgpu_b200.distributed import (ReplicatedSuffixDrafter,
+                                            ShardedSuffixDrafter)
     cfg = dict(wl.CONFIG5_DRAFTER)
     cfg["global_capacity"] = 1 << lg
-    if world > 1:
-        from suffixgpu_b200.distributed import ShardedSuffixDrafter
+    if mode == "shards":
         d = ShardedSuffixDrafter(device=dev, **cfg)
+    elif world > 1:
+        d = ReplicatedSuffixDrafter(device=dev, **cfg)
     else:
         d = SuffixGPUDrafter(device=dev, **cfg)
-    docs = torch.from_numpy(data["corpus_docs"]).to(dev)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     d.load_documents(list(docs.unbind(0)))
     torch.cuda.synchronize()
     load_s = time.perf_counter() - t0
-    del docs
     b = data["token_ids"].shape[0]
     tok0 = torch.from_numpy(data["token_ids"]).to(dev)
     q0 = torch.from_numpy(data["num_tokens"]).to(dev)
@@ -588,49 +630,90 @@ def run_sharded(args, dev, world: int, rank: int) -> dict | None:
                      "samp": torch.roll(samp0, 5 * r, 1).contiguous()})
     cycle = NREP5 * DECODE5
 
-    def run_seq(n):
+    def run_seq(n, marks=None):
         cur = [rp["cnt0"] for rp in reps]
+        if marks:
+            marks[0].record()
         for i in range(n):
             r, j = i % NREP5, (i // NREP5) % DECODE5
             if j == 0:
                 cur[r] = reps[r]["cnt0"]
             _, _, cur[r] = d.propose_with_update(cur[r], reps[r]["tok"],
                                                  reps[r]["samp"][j])
+        if marks:
+            marks[1].record()
 
     run_seq(3 * NREP5)
     torch.cuda.synchronize()
-    steps = max(1, args.sharded_steps)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        run_seq(min(steps, cycle))
-    graph.replay()
-    torch.cuda.synchronize()
-    reps_needed = max(1, steps // cycle)
-    steps = reps_needed * min(steps, cycle)
-    def replays():
-        for _ in range(reps_needed):
-            graph.replay()
-
-    ms_ranks = ranks_ms(device_window(replays, world), world, dev)
+    steps = max(1, min(args.sharded_steps, cycle))
+    phases = None
+    if mode == "shards":
+        # per-phase device times of a few eager steps
+        d.phase_events = []
+        run_seq(8)
+        torch.cuda.synchronize()
+        evs = d.phase_events
+        d.phase_events = None
+        acc: dict = {}
+        for i in range(1, len(evs)):
+            name, ev = evs[i]
+            if name == "start":
+                continue
+            acc.setdefault(name, []).append(evs[i - 1][1].elapsed_time(ev))
+        names = list(acc)
+        mine = [1e3 * sum(acc[k]) / len(acc[k]) for k in names]
+        allr = [max(ranks_ms(v, world, dev)) for v in mine]
+        phases = {"order": names,
+                  "us_rank0": mine if rank == 0 else None,
+                  "us_max_over_ranks": allr,
+                  "note": "eager steps, events between the step's phases on "
+                          "the current stream (collectives included)"}
+    marks = tuple(torch.cuda.Event(enable_timing=True, external=True)
+                  for _ in range(2))
+    graph = None
+    timing = "events recorded by the timed graph's first and last nodes"
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            run_seq(steps, marks)
+        graph.replay()
+        torch.cuda.synchronize()
+    except Exception as e:  # capture of the collectives refused: eager
+        graph = None
+        timing = f"eager steps in a busy-stream window ({type(e).__name__})"
+        torch.cuda.synchronize()
+    if graph is not None:
+        ms = device_window(graph.replay, world)
+        ms = marks[0].elapsed_time(marks[1])
+    else:
+        ms = device_window(lambda: run_seq(steps), world)
+    ms_ranks = ranks_ms(ms, world, dev)
     ms_max = max(ms_ranks)
     load_max = max(ranks_ms(load_s, world, dev))
     del graph
-    if rank != 0:
-        return None
-    return {"metric": "propose_with_update rows/s, global drafter "
-                      "(config 5)",
-            "value": world * b * steps / (ms_max * 1e-3), "unit": "rows/s",
-            "n_gpus": world, "rows_per_gpu": b, "steps": steps,
-            "ms_per_step": ms_max / steps, "scaling": "weak",
-            "ms_per_step_ranks": [m / steps for m in ms_ranks],
-            "corpus_tokens": int(d.global_index.active_len),
-            "load_s": load_max,
-            "workload": "config5: 128 rows x S=16384 per GPU, k=32, P=64, "
-                        "R=256, 8 backoff, factor 2.0, min_prob 0.1; "
-                        f"2^{lg}-token corpus of 512 x 512 templates (5% "
-                        "substitution, vocab 128256), index replicated on "
-                        "every GPU",
-            "l2": "16 rotating replicas x 8 MiB token buffer"}
+    out = {"metric": "propose_with_update rows/s, global drafter "
+                     f"(config 5, {mode} suffix array)",
+           "value": world * b * steps / (ms_max * 1e-3), "unit": "rows/s",
+           "n_gpus": world, "rows_per_gpu": b, "steps": steps,
+           "ms_per_step": ms_max / steps, "scaling": "weak",
+           "ms_per_step_ranks": [m / steps for m in ms_ranks],
+           "timing": timing,
+           "corpus_tokens": int(d.global_index.active_len),
+           "load_s": load_max,
+           "workload": "config5: 128 rows x S=16384 per GPU, k=32, P=64, "
+                       "R=256, 8 backoff, factor 2.0, min_prob 0.1; "
+                       f"2^{lg}-token corpus of 512 x 512 templates (5% "
+                       "substitution, vocab 128256); "
+                       + ("suffix array split into one shard per GPU by "
+                          "corpus position (global ranks), tails "
+                          "all-gathered, bounds all-reduced, samples "
+                          "reduce-scattered" if mode == "shards" else
+                          "whole suffix array on every GPU"),
+           "l2": "16 rotating replicas x 8 MiB token buffer"}
+    if phases is not None:
+        out["phases"] = phases
+    del d
+    return out
 
 
 def run_global(args, dev) -> dict:

@@ -27,7 +27,8 @@ therefore collective: every rank calls them, possibly with nothing to add.
 The corpus itself, the delta and the suffix-array build are the same on
 every rank in both modes (the build is replicated; a distributed suffix
 sort is not part of this package). Works with NCCL (CUDA tensors); the
-ingestion helpers also run on gloo (host tensors).
+ingestion helpers also run on gloo (host tensors). Without an initialised
+process group both drafters run as the only rank of a one-GPU job.
 """
 
 from __future__ import annotations
@@ -105,19 +106,20 @@ class ReplicatedSuffixDrafter(SuffixGPUDrafter):
     collective."""
 
     def __init__(self, *args, group=None, **kwargs):
-        if not dist.is_initialized():
-            raise RuntimeError(f"{type(self).__name__} needs an initialised "
-                               "torch.distributed process group")
         super().__init__(*args, **kwargs)
         self.group = group
-        self.rank = dist.get_rank(group)
-        self.world_size = dist.get_world_size(group)
+        # without an initialised process group: one rank, no exchange
+        self._distributed = dist.is_initialized()
+        self.rank = dist.get_rank(group) if self._distributed else 0
+        self.world_size = dist.get_world_size(group) \
+            if self._distributed else 1
         if self.global_index is not None and self.world_size > 1:
             self.global_index.rebuild_agree = (
                 lambda done: agree_all(done, self.group))
 
     def _append_docs(self, docs: list[torch.Tensor]) -> None:
-        all_docs = exchange_documents(docs, self.group)
+        all_docs = exchange_documents(docs, self.group) \
+            if self._distributed else docs
         if all_docs:
             self.global_index.append_documents(all_docs)
 
@@ -212,6 +214,19 @@ class _Collectives:
                                    group=self.group)
 
 
+class _LocalCollectives:
+    """The collectives of a one-rank job: copies."""
+
+    def all_gather(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        out.copy_(inp)
+
+    def all_reduce_sum(self, t: torch.Tensor) -> None:
+        pass
+
+    def reduce_scatter_sum(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        out.copy_(inp)
+
+
 class ShardedSuffixDrafter(ReplicatedSuffixDrafter):
     """One rank of the multi-GPU global drafter with the suffix array split
     into per-rank shards (module docstring). Needs ``enable_global=True``;
@@ -225,7 +240,8 @@ class ShardedSuffixDrafter(ReplicatedSuffixDrafter):
             raise ValueError("ShardedSuffixDrafter needs enable_global=True")
         self.shard = SuffixArrayShard(self.global_index, self.rank,
                                       self.world_size)
-        self._comm = _Collectives(group)
+        self._comm = _Collectives(group) if self._distributed \
+            else _LocalCollectives()
         self._bufs: dict = {}
         self.phase_events = None  # set to a list to record per-phase events
 
