@@ -655,19 +655,23 @@ def _run_config5_mode(args, dev, world, rank, mode, data, docs, lg):
         evs = d.phase_events
         d.phase_events = None
         acc: dict = {}
-        for i in range(1, len(evs)):
-            name, ev = evs[i]
-            if name == "start":
-                continue
-            acc.setdefault(name, []).append(evs[i - 1][1].elapsed_time(ev))
+        last: dict = {}
+        for lane, name, ev in evs:
+            if name != "start" and lane in last:
+                acc.setdefault(f"{lane}:{name}", []).append(
+                    last[lane].elapsed_time(ev))
+            last[lane] = ev
         names = list(acc)
         mine = [1e3 * sum(acc[k]) / len(acc[k]) for k in names]
         allr = [max(ranks_ms(v, world, dev)) for v in mine]
         phases = {"order": names,
                   "us_rank0": mine if rank == 0 else None,
                   "us_max_over_ranks": allr,
-                  "note": "eager steps, events between the step's phases on "
-                          "the current stream (collectives included)"}
+                  "note": "eager steps; events between consecutive phases "
+                          "of each stream: chain = the shard chain on the "
+                          "side stream (collectives included), own = the "
+                          "rank's rows on the caller's stream (delta scan "
+                          "and local step overlap the chain)"}
     marks = tuple(torch.cuda.Event(enable_timing=True, external=True)
                   for _ in range(2))
     graph = None

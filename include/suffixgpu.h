@@ -437,6 +437,20 @@ int sg_shard_pack_rows(const int32_t* tails, const int64_t* tail_len,
                        const uint8_t* row_mask, int32_t batch,
                        int32_t max_len, int32_t* rows, sg_stream_t stream);
 
+/* Per packed row: out_len[b] = the longest l <= the tail length whose
+ * last-l-token pattern starts some suffix of this shard (0: none, or the
+ * row does not draft), or max_len + 1 when the tail holds a -1 token (a
+ * pattern can then match past the corpus end, where tokens read -1, and
+ * the found lengths need not be 1..L). The MAX over all shards is the
+ * whole corpus's longest match: since a match of l tokens leaves one of
+ * l - 1 tokens, the lengths found over the whole corpus are 1..that MAX,
+ * and suffix_match_backoff's best length for cap c (sa_search.py:150-163)
+ * is min(cap_c, MAX). One warp per row, binary search over l. */
+int sg_shard_longest(const int32_t* shard_sa, int64_t shard_n,
+                     const int32_t* corpus, int64_t corpus_n,
+                     const int32_t* rows, int32_t batch, int32_t max_len,
+                     int32_t* out_len, sg_stream_t stream);
+
 /* Per packed row b and length l = 1..max_len: out_bounds[b, l-1, 0..1] =
  * (lower, upper) of the tail's last l tokens over the shard's suffix array
  * shard_sa[0..shard_n) (positions into corpus[0..corpus_n)): the number of
@@ -444,11 +458,17 @@ int sg_shard_pack_rows(const int32_t* tails, const int64_t* tail_len,
  * search_interval bounds on that array (sa_search.py:66-107, comparator
  * :25-63 with the whole corpus's end). Zeros for rows that do not draft and
  * lengths beyond the tail. Summed over all shards of a corpus they equal
- * search_interval on the whole suffix array. max_len <= 128. */
+ * search_interval on the whole suffix array. With `longest` (the MAX of
+ * sg_shard_longest over the shards, [batch]) only the lengths
+ * min(caps[c], longest[b]) are searched (every length when longest[b] >
+ * max_len) and the others are zeros: enough for the per-cap selection.
+ * max_len <= 128. */
 int sg_shard_bounds(const int32_t* shard_sa, int64_t shard_n,
                     const int32_t* corpus, int64_t corpus_n,
                     const int32_t* rows, int32_t batch, int32_t max_len,
-                    int32_t* out_bounds, sg_stream_t stream);
+                    const int32_t* longest, const int64_t* caps,
+                    int32_t num_caps, int32_t* out_bounds,
+                    sg_stream_t stream);
 
 /* From the summed bounds (bounds_sum, every shard's sg_shard_bounds added)
  * and this shard's own (bounds_local), per row and cap: the best length

@@ -114,8 +114,11 @@ _SIGS: dict[str, list] = {
                          c_void_p, c_void_p, c_size_t, c_void_p],
     "sg_shard_pack_rows": [c_void_p, c_void_p, c_void_p, c_int32, c_int32,
                            c_void_p, c_void_p],
+    "sg_shard_longest": [c_void_p, c_int64, c_void_p, c_int64, c_void_p,
+                         c_int32, c_int32, c_void_p, c_void_p],
     "sg_shard_bounds": [c_void_p, c_int64, c_void_p, c_int64, c_void_p,
-                        c_int32, c_int32, c_void_p, c_void_p],
+                        c_int32, c_int32, c_void_p, c_void_p, c_int32,
+                        c_void_p, c_void_p],
     "sg_shard_resolve": [c_void_p, c_void_p, c_void_p, c_int32, c_int32,
                          c_void_p, c_int32, c_int32, c_void_p, c_void_p,
                          c_void_p, c_int32, c_int32, c_void_p, c_void_p,

@@ -416,12 +416,28 @@ __global__ void __cluster_dims__(kSCG, 1, 1) __launch_bounds__(512)
 // length, drafting flag] int32. The bounds count the shard's suffixes
 // below the pattern (lower) and not above it (upper), so summing them over
 // all shards gives the whole-corpus interval.
+// Whether length l's bounds are needed by the per-cap selection, given the
+// row's longest matching length lstar over all shards (sg_shard_longest
+// summed with a MAX; M + 1 = every length): found lengths are then exactly
+// 1..lstar, so cap c selects min(cap_c, lstar).
+__device__ __forceinline__ bool length_needed(int l, int lstar, int M,
+                                              const int64_t* caps, int C) {
+  if (lstar > M) return true;
+  for (int c = 0; c < C; ++c) {
+    const int64_t want = caps[c] < lstar ? caps[c] : lstar;
+    if (want == l) return true;
+  }
+  return false;
+}
+
 template <int NC>
 __global__ void __launch_bounds__(kSWarps * 32)
     shard_bounds_kernel(const int32_t* __restrict__ sa, int64_t ns,
                         const int32_t* __restrict__ corpus, int64_t nc,
                         const int32_t* __restrict__ rows, int B, int W, int M,
-                        int iters, int32_t* __restrict__ out) {
+                        int iters, const int32_t* __restrict__ lstar,
+                        const int64_t* __restrict__ caps, int C,
+                        int32_t* __restrict__ out) {
   const int64_t w = static_cast<int64_t>(blockIdx.x) * kSWarps + warp_id();
   if (w >= static_cast<int64_t>(B) * M) return;  // warp-uniform
   const int b = static_cast<int>(w / M), l = static_cast<int>(w % M) + 1;
@@ -429,7 +445,8 @@ __global__ void __launch_bounds__(kSWarps * 32)
   const int32_t* row = rows + static_cast<int64_t>(b) * W;
   const int tl = row[M], active = row[M + 1];
   int64_t lo = 0, hi = 0;
-  if (active && l <= tl && ns > 0) {
+  const bool needed = !lstar || length_needed(l, lstar[b], M, caps, C);
+  if (active && l <= tl && ns > 0 && needed) {
     int pc[NC];
     const int o = tl - l;
 #pragma unroll
@@ -445,6 +462,53 @@ __global__ void __launch_bounds__(kSWarps * 32)
     out[2 * w] = static_cast<int32_t>(lo);
     out[2 * w + 1] = static_cast<int32_t>(hi);
   }
+}
+
+// The longest l <= tail length with the tail's last l tokens starting some
+// suffix of this shard (0: none), one warp per packed row. Found lengths
+// form a prefix 1..L (a match of l tokens at p leaves one of l - 1 tokens
+// at p + 1) unless a pattern can match past the corpus end, where tokens
+// read -1: rows whose tail holds a -1 report M + 1 (every length needed).
+// The row's longest over all shards is the MAX of the shards' values.
+template <int NC>
+__global__ void __launch_bounds__(kSWarps * 32)
+    shard_longest_kernel(const int32_t* __restrict__ sa, int64_t ns,
+                         const int32_t* __restrict__ corpus, int64_t nc,
+                         const int32_t* __restrict__ rows, int B, int W,
+                         int M, int32_t* __restrict__ out) {
+  const int b = blockIdx.x * kSWarps + warp_id();
+  if (b >= B) return;  // warp-uniform
+  const int lane = lane_id();
+  const int32_t* row = rows + static_cast<int64_t>(b) * W;
+  const int tl = row[M] < M ? row[M] : M, active = row[M + 1];
+  int best = 0;
+  bool minus_one = false;
+  for (int j = lane; j < tl; j += 32) minus_one |= row[j] == -1;
+  minus_one = __any_sync(SG_FULL_MASK, minus_one);
+  if (active && tl > 0 && minus_one) {
+    best = M + 1;
+  } else if (active && tl > 0 && ns > 0) {
+    int a = 0, z = tl;  // found(a) holds; the longest is in [a, z]
+    while (a < z) {
+      const int l = (a + z + 1) >> 1;
+      int pc[NC];
+      const int o = tl - l;
+#pragma unroll
+      for (int k = 0; k < NC; ++k) {
+        const int j = lane + 32 * k;
+        pc[k] = j < l ? row[o + j] : 0;
+      }
+      int64_t lo, hi;
+      warp_bounds<NC>(sa, corpus, ns, sa_iters(ns), pc, M, l, lo, hi, nc);
+      if (hi > lo) {
+        a = l;
+      } else {
+        z = l - 1;
+      }
+    }
+    best = a;
+  }
+  if (lane == 0) out[b] = best;
 }
 
 template <int NC>
@@ -554,15 +618,44 @@ extern "C" int sg_suffix_match_backoff(
   return check_launch();
 }
 
-extern "C" int sg_shard_bounds(const int32_t* shard_sa, int64_t shard_n,
-                               const int32_t* corpus, int64_t corpus_n,
-                               const int32_t* rows, int32_t batch,
-                               int32_t max_len, int32_t* out_bounds,
-                               sg_stream_t stream) {
-  sg::NvtxScope nvtx_range("sg_shard_bounds");
+extern "C" int sg_shard_longest(const int32_t* shard_sa, int64_t shard_n,
+                                const int32_t* corpus, int64_t corpus_n,
+                                const int32_t* rows, int32_t batch,
+                                int32_t max_len, int32_t* out_len,
+                                sg_stream_t stream) {
+  sg::NvtxScope nvtx_range("sg_shard_longest");
   if (shard_n < 0 || corpus_n < 1 || corpus_n > INT32_MAX ||
       shard_n > corpus_n || batch < 0 || max_len < 1 ||
       max_len > 32 * kSMaxCols)
+    return SG_ERR_INVALID;
+  if (batch == 0) return SG_OK;
+  if ((shard_n > 0 && !shard_sa) || !corpus || !rows || !out_len)
+    return SG_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned blocks = static_cast<unsigned>((batch + kSWarps - 1) / kSWarps);
+  const int W = max_len + 2;
+  if (max_len <= 32)
+    shard_longest_kernel<1><<<blocks, kSWarps * 32, 0, st>>>(
+        shard_sa, shard_n, corpus, corpus_n, rows, batch, W, max_len, out_len);
+  else if (max_len <= 64)
+    shard_longest_kernel<2><<<blocks, kSWarps * 32, 0, st>>>(
+        shard_sa, shard_n, corpus, corpus_n, rows, batch, W, max_len, out_len);
+  else
+    shard_longest_kernel<4><<<blocks, kSWarps * 32, 0, st>>>(
+        shard_sa, shard_n, corpus, corpus_n, rows, batch, W, max_len, out_len);
+  return check_launch();
+}
+
+extern "C" int sg_shard_bounds(const int32_t* shard_sa, int64_t shard_n,
+                               const int32_t* corpus, int64_t corpus_n,
+                               const int32_t* rows, int32_t batch,
+                               int32_t max_len, const int32_t* longest,
+                               const int64_t* caps, int32_t num_caps,
+                               int32_t* out_bounds, sg_stream_t stream) {
+  sg::NvtxScope nvtx_range("sg_shard_bounds");
+  if (shard_n < 0 || corpus_n < 1 || corpus_n > INT32_MAX ||
+      shard_n > corpus_n || batch < 0 || max_len < 1 ||
+      max_len > 32 * kSMaxCols || (longest && (!caps || num_caps < 1)))
     return SG_ERR_INVALID;
   if (batch == 0) return SG_OK;
   if ((shard_n > 0 && !shard_sa) || !corpus || !rows || !out_bounds)
@@ -575,14 +668,14 @@ extern "C" int sg_shard_bounds(const int32_t* shard_sa, int64_t shard_n,
   if (max_len <= 32)
     shard_bounds_kernel<1><<<blocks, kSWarps * 32, 0, st>>>(
         shard_sa, shard_n, corpus, corpus_n, rows, batch, W, max_len, it,
-        out_bounds);
+        longest, caps, num_caps, out_bounds);
   else if (max_len <= 64)
     shard_bounds_kernel<2><<<blocks, kSWarps * 32, 0, st>>>(
         shard_sa, shard_n, corpus, corpus_n, rows, batch, W, max_len, it,
-        out_bounds);
+        longest, caps, num_caps, out_bounds);
   else
     shard_bounds_kernel<4><<<blocks, kSWarps * 32, 0, st>>>(
         shard_sa, shard_n, corpus, corpus_n, rows, batch, W, max_len, it,
-        out_bounds);
+        longest, caps, num_caps, out_bounds);
   return check_launch();
 }

@@ -162,16 +162,18 @@ __global__ void pack_rows_kernel(const int32_t* __restrict__ tails,
 constexpr int kResolveThreads = 256;
 constexpr int kResolveMaxCaps = 16;
 
-// One block per row (every row of the job). Per cap the reference's best
+// One block per (row, cap), for every row of the job. The cap's best
 // length (suffix_match_backoff, sa_search.py:150-163: the longest length
-// <= cap and <= the tail length whose interval is not empty) from the
-// summed bounds; caps whose best length equals the previous cap's share
-// its samples. Then every sample slot [row, cap, j < R] gets the sample's
-// corpus position when this shard holds the suffix of that global rank,
-// else 0. For the rows this GPU drafts ([own_lo, own_lo + own_n)) the
-// fused global step's per-cap inputs are written: SA length, and a
-// [start, end) range of its sample block (min(ilen, R) entries, so the
-// step reads them in order).
+// <= cap and <= the tail length whose summed interval is not empty); caps
+// whose best length equals the previous cap's share its samples. Every
+// sample slot [row, cap, j < R] gets the sample's corpus position when
+// this shard holds the suffix of that global rank, else 0. A shard holding
+// few suffixes of the interval walks them (a suffix of global rank
+// start + d is sample j when d == floor(j * ilen / R)); otherwise each
+// sample's global rank is searched among them. For the rows this GPU
+// drafts ([own_lo, own_lo + own_n)) the fused global step's per-cap inputs
+// are written: SA length, and a [start, end) range of the sample block
+// (min(ilen, R) entries, so the step reads them in order).
 __global__ void __launch_bounds__(kResolveThreads)
     shard_resolve_kernel(const int32_t* __restrict__ gb,
                          const int32_t* __restrict__ lb,
@@ -183,74 +185,92 @@ __global__ void __launch_bounds__(kResolveThreads)
                          int64_t* __restrict__ sa_len,
                          int64_t* __restrict__ sa_start,
                          int64_t* __restrict__ sa_end) {
-  __shared__ int s_best[kResolveMaxCaps], s_src[kResolveMaxCaps];
-  const int b = blockIdx.x;
+  extern __shared__ int32_t s_out[];  // [R]
+  __shared__ int s_best[kResolveMaxCaps], s_src;
+  const int b = blockIdx.x, c = blockIdx.y;
   const int32_t* row = rows + static_cast<int64_t>(b) * (M + 2);
   const int32_t* g = gb + static_cast<int64_t>(b) * M * 2;
   const int32_t* l = lb + static_cast<int64_t>(b) * M * 2;
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
     const int tl = row[M], active = row[M + 1];
-    int prev = -1;
-    for (int c = 0; c < C; ++c) {
+    if (lane < C && lane <= c) {
       int best = 0;
       if (active) {
-        const int64_t cap = caps[c];
+        const int64_t cap = caps[lane];
         for (int len = 1; len <= M; ++len)
           if (len <= cap && len <= tl && g[2 * len - 1] > g[2 * len - 2])
             best = len;
       }
-      s_best[c] = best;
-      // first cap with this best length: the block whose samples it uses
-      s_src[c] = (c > 0 && best == s_best[c - 1]) ? s_src[c - 1] : c;
-      (void)prev;
+      s_best[lane] = best;
+    }
+    __syncwarp();
+    if (lane == 0) {
+      // first cap of the run of caps with this best length
+      int src = c;
+      while (src > 0 && s_best[src - 1] == s_best[c]) --src;
+      s_src = src;
     }
   }
   __syncthreads();
+  const int best = s_best[c];
+  const int src = s_src;
   const int64_t own = static_cast<int64_t>(b) - own_lo;
-  if (own >= 0 && own < own_n && threadIdx.x < C) {
-    const int c = threadIdx.x, best = s_best[c];
+  int64_t start = 0, ilen = 0;
+  if (best > 0) {
+    start = g[2 * best - 2];
+    ilen = static_cast<int64_t>(g[2 * best - 1]) - start;
+  }
+  const int64_t cnt = ilen < R ? ilen : R;
+  if (own >= 0 && own < own_n && threadIdx.x == 0) {
     const int64_t o = own * C + c;
     sa_len[o] = best;
-    int64_t st = 0, en = 0;
-    if (best > 0) {
-      const int64_t ilen = static_cast<int64_t>(g[2 * best - 1]) -
-                           g[2 * best - 2];
-      st = (own * C + s_src[c]) * R;
-      en = st + (ilen < R ? ilen : R);
-    }
+    const int64_t st = best > 0 ? (own * C + src) * R : 0;
     sa_start[o] = st;
-    sa_end[o] = en;
+    sa_end[o] = best > 0 ? st + cnt : 0;
   }
-  for (int c = 0; c < C; ++c) {
-    const int best = s_best[c];
-    int32_t* out = samples + (static_cast<int64_t>(b) * C + c) * R;
-    if (best == 0 || s_src[c] != c) {
-      for (int j = threadIdx.x; j < R; j += kResolveThreads) out[j] = 0;
-      continue;
-    }
-    const int64_t start = g[2 * best - 2];
-    const int64_t ilen = static_cast<int64_t>(g[2 * best - 1]) - start;
-    const int64_t cnt = ilen < R ? ilen : R;
-    const int64_t lo = l[2 * best - 2], hi = l[2 * best - 1];
-    for (int j = threadIdx.x; j < R; j += kResolveThreads) {
-      int32_t v = 0;
-      if (j < cnt && hi > lo) {
-        const int64_t want =
-            start + (ilen > R ? (static_cast<int64_t>(j) * ilen) / R : j);
-        // this shard's suffixes of the interval, ascending global ranks
-        int64_t a = lo, z = hi;
-        while (a < z) {
-          const int64_t m = (a + z) >> 1;
-          if (shard_rank[m] < want) {
-            a = m + 1;
-          } else {
-            z = m;
-          }
-        }
-        if (a < hi && shard_rank[a] == want) v = shard_pos[a];
+  int32_t* out = samples + (static_cast<int64_t>(b) * C + c) * R;
+  if (best == 0 || src != c) {
+    for (int j = threadIdx.x; j < R; j += kResolveThreads) out[j] = 0;
+    return;
+  }
+  const int64_t lo = l[2 * best - 2], hi = l[2 * best - 1];
+  if (hi - lo <= 4 * static_cast<int64_t>(R)) {
+    for (int j = threadIdx.x; j < R; j += kResolveThreads) s_out[j] = 0;
+    __syncthreads();
+    for (int64_t k = lo + threadIdx.x; k < hi; k += kResolveThreads) {
+      const int64_t d = static_cast<int64_t>(shard_rank[k]) - start;
+      int64_t j;
+      if (ilen > R) {
+        j = (d * R + ilen - 1) / ilen;  // smallest j with j * ilen / R >= d
+        if (j >= R || (j * ilen) / R != d) continue;
+      } else {
+        j = d;
       }
-      out[j] = v;
+      s_out[j] = shard_pos[k];
     }
+    __syncthreads();
+    for (int j = threadIdx.x; j < R; j += kResolveThreads) out[j] = s_out[j];
+    return;
+  }
+  for (int j = threadIdx.x; j < R; j += kResolveThreads) {
+    int32_t v = 0;
+    if (j < cnt) {
+      const int64_t want =
+          start + (ilen > R ? (static_cast<int64_t>(j) * ilen) / R : j);
+      // this shard's suffixes of the interval, ascending global ranks
+      int64_t a = lo, z = hi;
+      while (a < z) {
+        const int64_t m = (a + z) >> 1;
+        if (shard_rank[m] < want) {
+          a = m + 1;
+        } else {
+          z = m;
+        }
+      }
+      if (a < hi && shard_rank[a] == want) v = shard_pos[a];
+    }
+    out[j] = v;
   }
 }
 
@@ -320,7 +340,13 @@ extern "C" int sg_shard_resolve(const int32_t* bounds_sum,
   if (!bounds_sum || !bounds_local || !rows || !caps || !samples ||
       (own_n > 0 && (!sa_len || !sa_start || !sa_end)))
     return SG_ERR_INVALID;
-  shard_resolve_kernel<<<batch, kResolveThreads, 0,
+  const size_t smem = static_cast<size_t>(max_occ) * 4;
+  static int cache[64] = {0};
+  const int rc = ensure_dyn_smem(shard_resolve_kernel, smem, cache);
+  if (rc != SG_OK) return rc;
+  shard_resolve_kernel<<<dim3(static_cast<unsigned>(batch),
+                              static_cast<unsigned>(num_caps)),
+                         kResolveThreads, smem,
                          reinterpret_cast<cudaStream_t>(stream)>>>(
       bounds_sum, bounds_local, rows, max_len, caps, num_caps, max_occ,
       shard_pos, shard_rank, samples, own_lo, own_n, sa_len, sa_start,

@@ -19,8 +19,11 @@ therefore collective: every rank calls them, possibly with nothing to add.
   ranks (whole-corpus intervals), resolves the reference's strided
   suffix-array samples on the shard that holds them, and returns each
   row's samples to its owner (a sum reduce-scatter); the owner drafts from
-  its copy of the corpus. Three collectives per step: all-gather (tails),
-  all-reduce (bounds), reduce-scatter (samples).
+  its copy of the corpus. Four collectives per step: all-gather (tails),
+  all-reduce MAX (each row's longest match, so that only the lengths the
+  caps select are searched), all-reduce SUM (their bounds), reduce-scatter
+  (samples). They run on a side stream while the local step and the delta
+  scan of the rank's own rows run on the caller's.
 * ``ReplicatedSuffixDrafter``: every rank holds the whole suffix array and
   its propose path has no collective.
 
@@ -168,17 +171,34 @@ class SuffixArrayShard:
              ptr(self.pos), ptr(self.rank), ptr(self._ws), self._ws.numel(),
              stream_of(ix.device))
 
+    def longest(self, rows: torch.Tensor, max_len: int,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+        """Per packed row, the longest tail suffix that starts one of this
+        shard's suffixes (sg_shard_longest): int32 [B]."""
+        b = rows.shape[0]
+        if out is None:
+            out = torch.empty(b, dtype=torch.int32, device=rows.device)
+        ix = self.index
+        call("sg_shard_longest", ptr(self.pos), self.size, ptr(ix.corpus),
+             ix.capacity, ptr(rows), b, max_len, ptr(out),
+             stream_of(ix.device))
+        return out
+
     def bounds(self, rows: torch.Tensor, max_len: int,
-               out: torch.Tensor | None = None) -> torch.Tensor:
+               out: torch.Tensor | None = None,
+               longest: torch.Tensor | None = None,
+               caps: torch.Tensor | None = None) -> torch.Tensor:
         """Per packed row and length, this shard's (lower, upper) bounds:
-        int32 [B, max_len, 2]."""
+        int32 [B, max_len, 2]; with ``longest`` (the job-wide longest match
+        per row) and ``caps``, only the lengths the caps select."""
         b = rows.shape[0]
         if out is None:
             out = torch.empty(b, max_len, 2, dtype=torch.int32,
                               device=rows.device)
         ix = self.index
         call("sg_shard_bounds", ptr(self.pos), self.size, ptr(ix.corpus),
-             ix.capacity, ptr(rows), b, max_len, ptr(out),
+             ix.capacity, ptr(rows), b, max_len, ptr(longest), ptr(caps),
+             0 if caps is None else caps.numel(), ptr(out),
              stream_of(ix.device))
         return out
 
@@ -209,6 +229,9 @@ class _Collectives:
     def all_reduce_sum(self, t: torch.Tensor) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
 
+    def all_reduce_max(self, t: torch.Tensor) -> None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+
     def reduce_scatter_sum(self, out: torch.Tensor, inp: torch.Tensor) -> None:
         dist.reduce_scatter_tensor(out, inp, op=dist.ReduceOp.SUM,
                                    group=self.group)
@@ -221,6 +244,9 @@ class _LocalCollectives:
         out.copy_(inp)
 
     def all_reduce_sum(self, t: torch.Tensor) -> None:
+        pass
+
+    def all_reduce_max(self, t: torch.Tensor) -> None:
         pass
 
     def reduce_scatter_sum(self, out: torch.Tensor, inp: torch.Tensor) -> None:
@@ -243,7 +269,9 @@ class ShardedSuffixDrafter(ReplicatedSuffixDrafter):
         self._comm = _Collectives(group) if self._distributed \
             else _LocalCollectives()
         self._bufs: dict = {}
-        self.phase_events = None  # set to a list to record per-phase events
+        self._side = None
+        # a list to collect (phase, event) pairs of eager steps, or None
+        self.phase_events = None
 
     # the local step, the global step's own-row parts, the exchange
     def propose_with_update(self, num_tokens_no_spec, token_ids_gpu,
@@ -277,6 +305,7 @@ class ShardedSuffixDrafter(ReplicatedSuffixDrafter):
                   "row_mask": torch.empty(b, dtype=torch.uint8, device=dev),
                   "rows_own": torch.empty(b, p + 2, **i32),
                   "rows_all": torch.empty(g * b, p + 2, **i32),
+                  "longest": torch.empty(g * b, **i32),
                   "bounds_local": torch.empty(g * b, p, 2, **i32),
                   "bounds_sum": torch.empty(g * b, p, 2, **i32),
                   "samples_all": torch.empty(g * b, cnum, r, **i32),
@@ -289,11 +318,22 @@ class ShardedSuffixDrafter(ReplicatedSuffixDrafter):
                 self._bufs[key] = st
         return st
 
-    def _mark(self, name: str) -> None:
+    def _streams(self):
+        """The side stream of the shard chain and its fork / join events
+        (created on first use, reused)."""
+        if self._side is None:
+            self._side = (torch.cuda.Stream(self.device),
+                          torch.cuda.Event(), torch.cuda.Event())
+        return self._side
+
+    def _mark(self, name: str, lane: str = "chain") -> None:
+        """Per-phase timing (eager): an event on the current stream; lane
+        names the stream's sequence of phases ("chain": the shard chain on
+        the side stream, "own": the rank's own rows)."""
         if self.phase_events is not None:
             ev = torch.cuda.Event(enable_timing=True)
             ev.record()
-            self.phase_events.append((name, ev))
+            self.phase_events.append((lane, name, ev))
 
     def _step(self, counts, token_ids, sampled, vc, limit, mask):
         gi = self.global_index
@@ -304,14 +344,15 @@ class ShardedSuffixDrafter(ReplicatedSuffixDrafter):
         cnum = caps.numel()
         r = gi.max_occurrences
         st = self._buffers(b, p, cnum, r)
-        stream = stream_of(dev)
         counts = ops.as_i32(counts)
         samp = None if sampled is None else ops.as_i32(sampled)
         vci = None if (sampled is None or vc is None) else ops.as_i32(vc)
         m8 = None if (sampled is not None or mask is None) \
             else mask.to(torch.uint8).contiguous()
-        self._mark("start")
-        # this rank's tails as the update leaves them, and its drafting mask
+        cur = torch.cuda.current_stream(dev)
+        stream = stream_of(dev)
+        # this rank's tails as the update leaves them (read before the local
+        # step's scatter) and its drafting mask, packed for the exchange
         call("sg_gather_tails_update", ptr(token_ids), token_ids.stride(0),
              s, ptr(counts), ptr(samp),
              0 if samp is None else samp.shape[1], ptr(vci), int(limit),
@@ -319,33 +360,47 @@ class ShardedSuffixDrafter(ReplicatedSuffixDrafter):
              ptr(st["row_mask"]), stream)
         call("sg_shard_pack_rows", ptr(st["tails"]), ptr(st["tail_len"]),
              ptr(st["row_mask"]), b, p, ptr(st["rows_own"]), stream)
-        # every rank's rows, searched on this shard, bounds summed
-        self._comm.all_gather(st["rows_all"], st["rows_own"])
-        self._mark("gather_tails")
-        self.shard.bounds(st["rows_all"], p, out=st["bounds_local"])
-        self._mark("shard_search")
-        st["bounds_sum"].copy_(st["bounds_local"])
-        self._comm.all_reduce_sum(st["bounds_sum"])
-        self._mark("sum_bounds")
-        self.shard.resolve(st["bounds_sum"], st["bounds_local"],
-                           st["rows_all"], caps, r, self.rank * b, b,
-                           st["samples_all"], st["plan"])
-        self._mark("resolve")
-        self._comm.reduce_scatter_sum(st["samples"].view(-1),
-                                      st["samples_all"].view(-1))
-        self._mark("return_samples")
-        # own rows: delta scan, local step (performs the update), global step
+        side, fork, join = self._streams()
+        self._mark("start", "own")
+        fork.record(cur)
+        side.wait_event(fork)
+        with torch.cuda.stream(side):
+            # every rank's rows on this shard; per row the job-wide longest
+            # match, then the bounds of the lengths the caps select, summed
+            self._mark("start")
+            self._comm.all_gather(st["rows_all"], st["rows_own"])
+            self._mark("gather_tails")
+            self.shard.longest(st["rows_all"], p, out=st["longest"])
+            self._mark("shard_longest")
+            self._comm.all_reduce_max(st["longest"])
+            self._mark("max_longest")
+            self.shard.bounds(st["rows_all"], p, out=st["bounds_local"],
+                              longest=st["longest"], caps=caps)
+            self._mark("shard_bounds")
+            st["bounds_sum"].copy_(st["bounds_local"])
+            self._comm.all_reduce_sum(st["bounds_sum"])
+            self._mark("sum_bounds")
+            self.shard.resolve(st["bounds_sum"], st["bounds_local"],
+                               st["rows_all"], caps, r, self.rank * b, b,
+                               st["samples_all"], st["plan"])
+            self._mark("resolve")
+            self._comm.reduce_scatter_sum(st["samples"].view(-1),
+                                          st["samples_all"].view(-1))
+            self._mark("return_samples")
+            join.record(side)
+        # own rows meanwhile: delta scan, local step (performs the update)
         d_len, d_pos, d_cnt = st["delta"]
         call("sg_delta_match_backoff", ptr(gi.delta), gi.delta_capacity,
              ptr(gi.delta_len_t), ptr(st["tails"]), b, p, ptr(st["tail_len"]),
              p, ptr(caps), cnum, r, ptr(st["row_mask"]), ptr(d_len),
              ptr(d_pos), ptr(d_cnt), stream)
-        self._mark("delta")
         o = self.local_kernel.run(counts, token_ids, sampled=samp,
                                   valid_count=vci, limit=limit,
                                   mask=None if samp is not None else mask,
                                   extras=True)
-        self._mark("local")
+        self._mark("delta_and_local", "own")
+        cur.wait_event(join)
+        self._mark("wait_for_chain", "own")
         sa_len, s_start, s_end = st["plan"]
         draft, nv = o["draft"], o["num_valid"]
         check("sg_global_draft_samples", lib().sg_global_draft_samples(
@@ -358,7 +413,7 @@ class ShardedSuffixDrafter(ReplicatedSuffixDrafter):
             float(self.min_token_prob), float(self.vote_smoothing_alpha),
             ptr(o["best_score"]), ptr(st["row_mask"]), ptr(draft), ptr(nv),
             stream))
-        self._mark("global_step")
+        self._mark("global_step", "own")
         return draft, nv, o.get("new_counts")
 
 

@@ -117,41 +117,98 @@ def test_extract_and_summed_bounds_equal_whole_index(parts):
     np.testing.assert_array_equal(total[..., 1][live], en.reshape(b, m)[live])
     assert (total[~live] == 0).all()
     assert (en - st).max() > 32  # intervals wider than R exist
+    # longest match: MAX over the shards = the longest found length (found
+    # lengths are a prefix 1..L), or M + 1 for a tail holding -1
+    found = live & (en > st).reshape(b, m)
+    exp_long = np.where(found.any(axis=1),
+                        m - np.argmax(found[:, ::-1], axis=1), 0)
+    for L in range(b):
+        assert found[L, :exp_long[L]].all(), L  # the prefix property
+    rows_d = _dev(rows.astype(np.int32))
+    longest = torch.stack([sh.longest(rows_d, m) for sh in shards]).amax(0)
+    np.testing.assert_array_equal(_host(longest), exp_long)
+    rows_neg = rows.copy()
+    rows_neg[5, int(tlen[5]) - 1] = -1 if tlen[5] > 0 else 0
+    if tlen[5] > 0:
+        lneg = torch.stack([sh.longest(_dev(rows_neg.astype(np.int32)), m)
+                            for sh in shards]).amax(0)
+        assert int(lneg[5]) == m + 1
+    # bounds of the cap-selected lengths only
+    caps = np.array([16, 8, 4, 2], dtype=np.int64)
+    sel = None
+    for sh in shards:
+        bd = sh.bounds(rows_d, m, longest=longest, caps=_dev(caps))
+        sel = bd.to(torch.int64) if sel is None else sel + bd
+    sel = _host(sel)
+    for bi in range(b):
+        need = {int(min(c, exp_long[bi])) for c in caps} - {0}
+        for li in range(m):
+            if li + 1 in need:
+                np.testing.assert_array_equal(sel[bi, li], total[bi, li])
+            else:
+                assert (sel[bi, li] == 0).all()
 
 
 class _ThreadComm:
-    """Collectives among threads standing in for ranks: every rank hands
-    in its tensor, waits for the others, and combines on the one CUDA
-    stream they share (host barriers order the launches)."""
+    """Collectives among threads standing in for ranks. Each rank hands in
+    its tensor with an event on its current stream; after a barrier every
+    rank's current stream waits for all those events, combines, and records
+    a second event; after a second barrier every stream waits for all of
+    those, so that no rank overwrites an input another is still reading
+    (the synchronisation a real collective gives its streams)."""
 
     def __init__(self, world: int):
         self.world = world
         self.barrier = threading.Barrier(world, timeout=120)
         self.slots = [None] * world
+        self.ready = [None] * world
+        self.done = [None] * world
+
+    def _run(self, rank, t, combine):
+        cur = torch.cuda.current_stream()
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        self.slots[rank], self.ready[rank] = t, ev
+        self.barrier.wait()
+        for e in self.ready:
+            cur.wait_event(e)
+        combine(self.slots)
+        ev2 = torch.cuda.Event()
+        ev2.record(cur)
+        self.done[rank] = ev2
+        self.barrier.wait()
+        for e in self.done:
+            cur.wait_event(e)
+        self.barrier.wait()  # slots free for the next collective
 
     def view(self, rank: int):
         comm = self
 
         class _R:
             def all_gather(self, out, inp):
-                comm.slots[rank] = inp
-                comm.barrier.wait()
-                torch.cat(comm.slots, dim=0, out=out)
-                comm.barrier.wait()
+                comm._run(rank, inp,
+                          lambda sl: torch.cat(sl, dim=0, out=out))
 
             def all_reduce_sum(self, t):
-                comm.slots[rank] = t.clone()
-                comm.barrier.wait()
-                t.copy_(sum(s.to(torch.int64) for s in comm.slots).to(t.dtype))
-                comm.barrier.wait()
+                src = t.clone()
+
+                def comb(sl):
+                    t.copy_(sum(x.to(torch.int64) for x in sl).to(t.dtype))
+                comm._run(rank, src, comb)
+
+            def all_reduce_max(self, t):
+                src = t.clone()
+                comm._run(rank, src,
+                          lambda sl: t.copy_(torch.stack(sl).amax(dim=0)))
 
             def reduce_scatter_sum(self, out, inp):
-                comm.slots[rank] = inp
-                comm.barrier.wait()
-                tot = sum(s.to(torch.int64) for s in comm.slots)
                 n = out.numel()
-                out.copy_(tot[rank * n:(rank + 1) * n].to(out.dtype))
-                comm.barrier.wait()
+
+                def comb(sl):
+                    tot = sum(x[rank * n:(rank + 1) * n].to(torch.int64)
+                              for x in sl)
+                    out.copy_(tot.to(out.dtype))
+                comm._run(rank, inp, comb)
         return _R()
 
 
