@@ -600,6 +600,23 @@ def run_sharded(args, dev, world: int, rank: int) -> dict | None:
     return out
 
 
+def _length_search_probe(d, run_seq, steps, world, dev) -> dict:
+    """Eager device time per step of the shards mode with each length
+    search (every length in one round / longest match first)."""
+    import torch
+    out = {}
+    keep = d.length_search
+    for ls in ("all", "longest"):
+        d.length_search = ls
+        run_seq(min(steps, 16))
+        torch.cuda.synchronize()
+        ms = device_window(lambda: run_seq(steps), world)
+        out[ls] = max(ranks_ms(ms, world, dev)) / steps * 1e3
+    d.length_search = keep
+    return {"us_per_step_eager": out,
+            "used": "longest" if d._longest_first() else "all"}
+
+
 def _run_config5_mode(args, dev, world, rank, mode, data, docs, lg):
     import torch
     from suffixgpu_b200 import SuffixGPUDrafter
@@ -672,6 +689,9 @@ def _run_config5_mode(args, dev, world, rank, mode, data, docs, lg):
                           "side stream (collectives included), own = the "
                           "rank's rows on the caller's stream (delta scan "
                           "and local step overlap the chain)"}
+    probe = None
+    if mode == "shards":
+        probe = _length_search_probe(d, run_seq, 64, world, dev)
     marks = tuple(torch.cuda.Event(enable_timing=True, external=True)
                   for _ in range(2))
     graph = None
@@ -716,6 +736,8 @@ def _run_config5_mode(args, dev, world, rank, mode, data, docs, lg):
            "l2": "16 rotating replicas x 8 MiB token buffer"}
     if phases is not None:
         out["phases"] = phases
+    if probe is not None:
+        out["length_search"] = probe
     del d
     return out
 

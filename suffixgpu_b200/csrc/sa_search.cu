@@ -465,32 +465,46 @@ __global__ void __launch_bounds__(kSWarps * 32)
 }
 
 // The longest l <= tail length with the tail's last l tokens starting some
-// suffix of this shard (0: none), one warp per packed row. Found lengths
-// form a prefix 1..L (a match of l tokens at p leaves one of l - 1 tokens
-// at p + 1) unless a pattern can match past the corpus end, where tokens
-// read -1: rows whose tail holds a -1 report M + 1 (every length needed).
-// The row's longest over all shards is the MAX of the shards' values.
+// suffix of this shard (0: none), one block of kSWarps warps per packed
+// row. Found lengths form a prefix 1..L (a match of l tokens at p leaves
+// one of l - 1 tokens at p + 1) unless a pattern can match past the corpus
+// end, where tokens read -1: rows whose tail holds a -1 report M + 1
+// (every length needed). The search keeps found(a) and !found(z + 1) and
+// probes kSWarps lengths of (a, z] at once per round (one per warp), so a
+// 64-token tail takes two rounds. The row's longest over all shards is the
+// MAX of the shards' values.
 template <int NC>
 __global__ void __launch_bounds__(kSWarps * 32)
     shard_longest_kernel(const int32_t* __restrict__ sa, int64_t ns,
                          const int32_t* __restrict__ corpus, int64_t nc,
-                         const int32_t* __restrict__ rows, int B, int W,
-                         int M, int32_t* __restrict__ out) {
-  const int b = blockIdx.x * kSWarps + warp_id();
-  if (b >= B) return;  // warp-uniform
-  const int lane = lane_id();
+                         const int32_t* __restrict__ rows, int W, int M,
+                         int32_t* __restrict__ out) {
+  __shared__ int s_found[kSWarps], s_len[kSWarps];
+  __shared__ int s_a, s_z;
+  const int b = blockIdx.x;
+  const int warp = warp_id(), lane = lane_id();
   const int32_t* row = rows + static_cast<int64_t>(b) * W;
   const int tl = row[M] < M ? row[M] : M, active = row[M + 1];
-  int best = 0;
-  bool minus_one = false;
-  for (int j = lane; j < tl; j += 32) minus_one |= row[j] == -1;
-  minus_one = __any_sync(SG_FULL_MASK, minus_one);
-  if (active && tl > 0 && minus_one) {
-    best = M + 1;
-  } else if (active && tl > 0 && ns > 0) {
-    int a = 0, z = tl;  // found(a) holds; the longest is in [a, z]
-    while (a < z) {
-      const int l = (a + z + 1) >> 1;
+  if (threadIdx.x < 32) {
+    bool minus_one = false;
+    for (int j = lane; j < tl; j += 32) minus_one |= row[j] == -1;
+    minus_one = __any_sync(SG_FULL_MASK, minus_one);
+    if (lane == 0) {
+      s_a = 0;
+      s_z = (active && tl > 0 && ns > 0) ? tl : 0;
+      if (active && tl > 0 && minus_one) s_a = s_z = M + 1;
+    }
+  }
+  __syncthreads();
+  while (s_a < s_z) {  // block-uniform
+    const int a = s_a, z = s_z, span = z - a;
+    // probe lengths a < l_0 < ... <= z, spread over the span
+    const int l = span <= kSWarps
+                      ? (warp < span ? a + warp + 1 : 0)
+                      : a + static_cast<int>((static_cast<int64_t>(warp + 1) *
+                                              span + kSWarps - 1) / kSWarps);
+    int found = 0;
+    if (l > 0) {
       int pc[NC];
       const int o = tl - l;
 #pragma unroll
@@ -500,15 +514,29 @@ __global__ void __launch_bounds__(kSWarps * 32)
       }
       int64_t lo, hi;
       warp_bounds<NC>(sa, corpus, ns, sa_iters(ns), pc, M, l, lo, hi, nc);
-      if (hi > lo) {
-        a = l;
-      } else {
-        z = l - 1;
-      }
+      found = hi > lo;
     }
-    best = a;
+    if (lane == 0) {
+      s_found[warp] = found;
+      s_len[warp] = l;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int na = a, nz = z;
+      for (int w = 0; w < kSWarps; ++w) {
+        if (s_len[w] == 0) continue;
+        if (s_found[w]) {
+          if (s_len[w] > na) na = s_len[w];
+        } else if (s_len[w] - 1 < nz) {
+          nz = s_len[w] - 1;
+        }
+      }
+      s_a = na;
+      s_z = nz;
+    }
+    __syncthreads();
   }
-  if (lane == 0) out[b] = best;
+  if (threadIdx.x == 0) out[b] = s_a;
 }
 
 template <int NC>
@@ -632,17 +660,17 @@ extern "C" int sg_shard_longest(const int32_t* shard_sa, int64_t shard_n,
   if ((shard_n > 0 && !shard_sa) || !corpus || !rows || !out_len)
     return SG_ERR_INVALID;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const unsigned blocks = static_cast<unsigned>((batch + kSWarps - 1) / kSWarps);
+  const unsigned blocks = static_cast<unsigned>(batch);
   const int W = max_len + 2;
   if (max_len <= 32)
     shard_longest_kernel<1><<<blocks, kSWarps * 32, 0, st>>>(
-        shard_sa, shard_n, corpus, corpus_n, rows, batch, W, max_len, out_len);
+        shard_sa, shard_n, corpus, corpus_n, rows, W, max_len, out_len);
   else if (max_len <= 64)
     shard_longest_kernel<2><<<blocks, kSWarps * 32, 0, st>>>(
-        shard_sa, shard_n, corpus, corpus_n, rows, batch, W, max_len, out_len);
+        shard_sa, shard_n, corpus, corpus_n, rows, W, max_len, out_len);
   else
     shard_longest_kernel<4><<<blocks, kSWarps * 32, 0, st>>>(
-        shard_sa, shard_n, corpus, corpus_n, rows, batch, W, max_len, out_len);
+        shard_sa, shard_n, corpus, corpus_n, rows, W, max_len, out_len);
   return check_launch();
 }
 

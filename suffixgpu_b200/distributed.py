@@ -19,11 +19,12 @@ therefore collective: every rank calls them, possibly with nothing to add.
   ranks (whole-corpus intervals), resolves the reference's strided
   suffix-array samples on the shard that holds them, and returns each
   row's samples to its owner (a sum reduce-scatter); the owner drafts from
-  its copy of the corpus. Four collectives per step: all-gather (tails),
-  all-reduce MAX (each row's longest match, so that only the lengths the
-  caps select are searched), all-reduce SUM (their bounds), reduce-scatter
-  (samples). They run on a side stream while the local step and the delta
-  scan of the rank's own rows run on the caller's.
+  its copy of the corpus. Collectives per step: all-gather (tails),
+  all-reduce SUM (bounds), reduce-scatter (samples), and on larger jobs an
+  all-reduce MAX before the bounds (each row's longest match, so that only
+  the lengths the caps select are searched). They run on a side stream
+  while the local step and the delta scan of the rank's own rows run on
+  the caller's.
 * ``ReplicatedSuffixDrafter``: every rank holds the whole suffix array and
   its propose path has no collective.
 
@@ -270,6 +271,11 @@ class ShardedSuffixDrafter(ReplicatedSuffixDrafter):
             else _LocalCollectives()
         self._bufs: dict = {}
         self._side = None
+        # "all" (every length's bounds in one round), "longest" (the job-wide
+        # longest match first), or "auto": longest first from
+        # longest_first_from ranks on
+        self.length_search = "auto"
+        self.longest_first_from = 4
         # a list to collect (phase, event) pairs of eager steps, or None
         self.phase_events = None
 
@@ -317,6 +323,17 @@ class ShardedSuffixDrafter(ReplicatedSuffixDrafter):
             if not torch.cuda.is_current_stream_capturing():
                 self._bufs[key] = st
         return st
+
+    def _longest_first(self) -> bool:
+        """Whether the step searches each row's longest match first (two
+        rounds: a MAX, then only the cap-selected lengths' bounds) instead
+        of every length's bounds in one round. Every rank searches every
+        row of the job, so the saved search work grows with the world size
+        while the extra round costs a fixed latency."""
+        mode = self.length_search
+        if mode == "auto":
+            return self.world_size >= self.longest_first_from
+        return mode == "longest"
 
     def _streams(self):
         """The side stream of the shard chain and its fork / join events
@@ -370,12 +387,15 @@ class ShardedSuffixDrafter(ReplicatedSuffixDrafter):
             self._mark("start")
             self._comm.all_gather(st["rows_all"], st["rows_own"])
             self._mark("gather_tails")
-            self.shard.longest(st["rows_all"], p, out=st["longest"])
-            self._mark("shard_longest")
-            self._comm.all_reduce_max(st["longest"])
-            self._mark("max_longest")
-            self.shard.bounds(st["rows_all"], p, out=st["bounds_local"],
-                              longest=st["longest"], caps=caps)
+            if self._longest_first():
+                self.shard.longest(st["rows_all"], p, out=st["longest"])
+                self._mark("shard_longest")
+                self._comm.all_reduce_max(st["longest"])
+                self._mark("max_longest")
+                self.shard.bounds(st["rows_all"], p, out=st["bounds_local"],
+                                  longest=st["longest"], caps=caps)
+            else:
+                self.shard.bounds(st["rows_all"], p, out=st["bounds_local"])
             self._mark("shard_bounds")
             st["bounds_sum"].copy_(st["bounds_local"])
             self._comm.all_reduce_sum(st["bounds_sum"])

@@ -227,7 +227,7 @@ def _emulated_drafters(world: int, cfg: dict):
     return ds, comm
 
 
-def _run_emulated(sc: dict, world: int, prefill=None):
+def _run_emulated(sc: dict, world: int, prefill=None, mode="auto"):
     """Each emulated rank drafts its share of the rows and ingests every
     document itself (the ingestion exchange is not emulated: replicas stay
     identical because they receive the same documents)."""
@@ -235,6 +235,8 @@ def _run_emulated(sc: dict, world: int, prefill=None):
     b = data["token_ids"].shape[0]
     per = b // world
     ds, comm = _emulated_drafters(world, sc["drafter"])
+    for d in ds:
+        d.length_search = mode
     results = [None] * world
     errors = []
 
@@ -277,13 +279,14 @@ def _run_emulated(sc: dict, world: int, prefill=None):
     return results
 
 
+@pytest.mark.parametrize("mode", ["all", "longest"])
 @pytest.mark.parametrize("world", [2, 3])
 @pytest.mark.parametrize("seed", [41, 45])
-def test_emulated_ranks_match_oracle(world_one, world, seed):
+def test_emulated_ranks_match_oracle(world_one, world, seed, mode):
     sc = scenarios.global_scenario(seed, steps=10)
     exp = scenarios.run_scenario(sc, so.SuffixDrafter, lambda a: a.copy(),
                                  lambda a: np.asarray(a).copy())
-    got = _run_emulated(sc, world)
+    got = _run_emulated(sc, world, mode=mode)
     per = sc["data"]["token_ids"].shape[0] // world
     for r in range(world):
         rows = slice(r * per, (r + 1) * per)
@@ -293,7 +296,8 @@ def test_emulated_ranks_match_oracle(world_one, world, seed):
         np.testing.assert_array_equal(got[r]["sa"], exp["sa"])
 
 
-def test_emulated_ranks_config5_settings_match_oracle(world_one):
+@pytest.mark.parametrize("mode", ["all", "longest"])
+def test_emulated_ranks_config5_settings_match_oracle(world_one, mode):
     """Config 5's drafter (k = 32, P = 64, R = 256, caps 64..2) on 4
     emulated ranks over a 2^18-token template corpus, 3 decode steps with
     harvests between them."""
@@ -321,7 +325,7 @@ def test_emulated_ranks_config5_settings_match_oracle(world_one):
             dr, nv, n = o.propose_with_update(n, tok, data["sampled"][arg])
             exp["draft"].append(dr)
             exp["num_valid"].append(nv)
-    got = _run_emulated(sc, 4, prefill=docs)
+    got = _run_emulated(sc, 4, prefill=docs, mode=mode)
     for r in range(4):
         rows = slice(4 * r, 4 * r + 4)
         np.testing.assert_array_equal(got[r]["draft"],
