@@ -323,8 +323,9 @@ def run_ours(args):
     clock.start()
 
     def replays():
-        for _ in range(args.steps // cycle):
-            full.replay()
+        if full is not None:
+            for _ in range(args.steps // cycle):
+                full.replay()
         if part is not None:
             part.replay()
 
@@ -503,6 +504,19 @@ def run_sa(args, dev) -> dict:
     peaks = _peaks()
     achieved = alg / (ms * 1e-3) / 1e9
     queries = run_queries(args, tok, out, dev, peaks)
+    dram = _sa_traffic()
+    measured = None
+    if dram is not None:
+        # measured DRAM bytes of a 2^22 build, scaled by tokens x rounds
+        scaled = dram["bytes"] * (n / (1 << 22)) * (rounds / dram["rounds"])
+        gbs = scaled / (ms * 1e-3) / 1e9
+        measured = {"traffic_bytes_per_build": scaled,
+                    "achieved": gbs, "frac": gbs / peaks["hbm_gbs"],
+                    "unit": "GB/s",
+                    "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum "
+                              "of every launch of a 2^22 build "
+                              "(profiles/sa_build_config4.txt), scaled to "
+                              "this build by tokens x doubling rounds"}
     return {"metric": "SA build Mtok/s", "value": n / (ms * 1e-3) / 1e6,
             "unit": "Mtok/s", "n_tokens": n, "ms_per_build": ms,
             "doubling_rounds": rounds, "reps": len(times),
@@ -512,7 +526,8 @@ def run_sa(args, dev) -> dict:
                          "peak": peaks["hbm_gbs"],
                          "peak_source": peaks["source"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"],
-                         "alg_bytes_per_build": alg},
+                         "alg_bytes_per_build": alg,
+                         "measured_dram": measured},
             "sa_search": queries}
 
 
@@ -1066,6 +1081,22 @@ def _traffic():
 # ---------------------------------------------------------------------------
 # CPU baseline (oracle port of the reference's torch CPU path)
 # ---------------------------------------------------------------------------
+def _sa_traffic():
+    """Measured DRAM bytes of one 2^22 suffix-array build and its rounds,
+    from the committed ncu summary (profiles/sa_build_config4.txt)."""
+    path = os.path.join(ROOT, "profiles", "sa_build_config4.txt")
+    got = {}
+    try:
+        for ln in open(path):
+            if ln.startswith("dram_bytes_per_build_2^22:"):
+                got["bytes"] = float(ln.split(":")[1])
+            elif ln.startswith("dram_rounds_2^22:"):
+                got["rounds"] = float(ln.split(":")[1])
+    except OSError:
+        return None
+    return got if len(got) == 2 else None
+
+
 def _cpu_chunk(payload):
     rows, steps, warm, cfg = payload
     sys.path.insert(0, ROOT)
