@@ -615,6 +615,47 @@ def run_sharded(args, dev, world: int, rank: int) -> dict | None:
     return out
 
 
+def _phase_times(d, run_seq, world, dev) -> dict:
+    """Per-phase device times of the sharded step: 8 steps captured in a
+    CUDA graph with an event-record node between phases (eager steps when
+    capture is refused), averaged per phase, rank 0 and max over ranks.
+    Phases are timed per stream: "chain" is the shard chain on the side
+    stream (collectives included), "own" the rank's rows on the caller's
+    stream (delta scan and local step overlap the chain)."""
+    import torch
+    d.phase_events = []
+    how = "CUDA graph with event-record nodes"
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            run_seq(8)
+        evs = d.phase_events
+        d.phase_events = None
+        g.replay()
+        torch.cuda.synchronize()
+    except Exception as e:  # capture refused: eager steps
+        d.phase_events = []
+        run_seq(8)
+        torch.cuda.synchronize()
+        evs = d.phase_events
+        how = f"eager steps ({type(e).__name__} in capture)"
+        g = None
+    d.phase_events = None
+    acc: dict = {}
+    last: dict = {}
+    for lane, name, ev in evs:
+        if name != "start" and lane in last:
+            acc.setdefault(f"{lane}:{name}", []).append(
+                last[lane].elapsed_time(ev))
+        last[lane] = ev
+    names = list(acc)
+    mine = [1e3 * sum(acc[k]) / len(acc[k]) for k in names]
+    allr = [max(ranks_ms(v, world, dev)) for v in mine]
+    del g
+    return {"order": names, "us_rank0": mine, "us_max_over_ranks": allr,
+            "how": how}
+
+
 def _length_search_probe(d, run_seq, steps, world, dev) -> dict:
     """Eager device time per step of the shards mode with each length
     search (every length in one round / longest match first)."""
@@ -680,30 +721,7 @@ def _run_config5_mode(args, dev, world, rank, mode, data, docs, lg):
     steps = max(1, min(args.sharded_steps, cycle))
     phases = None
     if mode == "shards":
-        # per-phase device times of a few eager steps
-        d.phase_events = []
-        run_seq(8)
-        torch.cuda.synchronize()
-        evs = d.phase_events
-        d.phase_events = None
-        acc: dict = {}
-        last: dict = {}
-        for lane, name, ev in evs:
-            if name != "start" and lane in last:
-                acc.setdefault(f"{lane}:{name}", []).append(
-                    last[lane].elapsed_time(ev))
-            last[lane] = ev
-        names = list(acc)
-        mine = [1e3 * sum(acc[k]) / len(acc[k]) for k in names]
-        allr = [max(ranks_ms(v, world, dev)) for v in mine]
-        phases = {"order": names,
-                  "us_rank0": mine if rank == 0 else None,
-                  "us_max_over_ranks": allr,
-                  "note": "eager steps; events between consecutive phases "
-                          "of each stream: chain = the shard chain on the "
-                          "side stream (collectives included), own = the "
-                          "rank's rows on the caller's stream (delta scan "
-                          "and local step overlap the chain)"}
+        phases = _phase_times(d, run_seq, world, dev)
     probe = None
     if mode == "shards":
         probe = _length_search_probe(d, run_seq, 64, world, dev)

@@ -174,6 +174,9 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
 
   __shared__ long long s_q, s_base, s_cnt;
   __shared__ int s_mask, s_nload, s_nal;
+  // the best selection value among the candidates finished so far, as an
+  // order-preserving key (0 = none yet)
+  __shared__ unsigned s_best_key;
 
   const int b = blockIdx.x;
   const int t = threadIdx.x;
@@ -264,6 +267,7 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
     if (lane == 0) {
       s_q = q; s_base = base; s_cnt = cnt; s_mask = m;
       s_nload = nload; s_nal = nal;
+      s_best_key = 0u;
     }
   } else {
     // other warps: empty the vote tables (warp 1 also warp 0's) and the
@@ -570,12 +574,42 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
       const int x = e + d;  // e < S < 2^23, d < 64
       return x < q32 ? tok_s[x < S ? x : S - 1] : -1;
     };
+    // The selection (step 4) takes the first maximum of score + f32(cand)
+    // * 1e-6. With alpha >= 0 a depth's ratio count / (active + alpha) is
+    // at most 1, so the chain probability never grows and the final score
+    // is at most score + rem * prob (rem = scored depths left). A
+    // candidate whose bound, with a margin above fp32 rounding, is below
+    // the value a finished candidate already reached cannot be selected
+    // and stops voting; its outputs are never read.
+    const float tie = __fmul_rn(static_cast<float>(cand), 1e-6f);
+    const bool may_stop = p.vote_alpha >= 0.0f;
+    auto stop = [&](float score, float prob, int d, int rem) -> bool {
+      (void)d;
+      const unsigned kb = *reinterpret_cast<volatile unsigned*>(&s_best_key);
+      if (!may_stop || kb == 0u) return false;
+      const uint32_t bits = (kb & 0x80000000u) ? (kb & 0x7fffffffu) : ~kb;
+      const float best = __uint_as_float(bits);
+      // rounded up at every step: above the exact score + rem * prob +
+      // tie, and the 1e-5 covers the fp32 rounding of the real sums
+      float ub = __fadd_ru(__fadd_ru(score, __fmul_ru(static_cast<float>(rem),
+                                                      prob)), tie);
+      ub = __fadd_ru(__fmul_ru(ub, 1.00001f), 1e-30f);
+      return ub < best;
+    };
     const ExpandResult er = warp_expand<RJ>(
         key_of, cont, n, K, spec_cap(p, cand), /*stop_at_cap=*/true,
-        p.min_token_prob, p.vote_alpha, vs, chain);
+        p.min_token_prob, p.vote_alpha, vs, chain, stop);
     if (lane == 0) {
-      score_s[c] = er.score;
-      emit_s[c] = er.emit;
+      if (er.stopped) {
+        score_s[c] = -INFINITY;  // never the maximum (see the rule above)
+        emit_s[c] = 0;
+      } else {
+        score_s[c] = er.score;
+        emit_s[c] = er.emit;
+        const float v = __fadd_rn(__fadd_rn(er.score, tie), 0.0f);
+        const uint32_t vb = __float_as_uint(v);
+        atomicMax(&s_best_key, (vb & 0x80000000u) ? ~vb : (vb | 0x80000000u));
+      }
     }
   }
   __syncthreads();

@@ -21,8 +21,8 @@
 //     open-addressing table in shared memory, one CAS insert + one atomic
 //     add per token, all of a lane's in flight together; every lane then
 //     empties the slots it used.
-// The winner's non-matching occurrences drop their alive bit; once <= 32
-// remain they are compacted to one per lane. While all survivors agree, up
+// The winner's non-matching occurrences drop their alive bit; whenever the
+// survivors fit fewer slots they are compacted (one per lane at <= 32). While all survivors agree, up
 // to 8 depths are committed at once from a shared lookahead.
 #pragma once
 
@@ -34,6 +34,14 @@ struct ExpandResult {
   int num_valid;  // leading valid depths (computed ones when stopping at cap)
   int emit;       // min(num_valid, max(cap, 0))
   float score;
+  bool stopped;   // given up early (the stop rule said it cannot win)
+};
+
+// Stop rule of warp_expand that never stops.
+struct NeverStop {
+  __device__ __forceinline__ bool operator()(float, float, int, int) const {
+    return false;
+  }
 };
 
 // Per-warp shared-memory scratch for the vote.
@@ -227,11 +235,16 @@ __device__ __forceinline__ void vote_multi(const int (&v)[RJ], int nslots,
 //                operator, which also returns num_valid, does not.
 //   chain_out: K ints; entries past the last computed depth are -1.
 // RJ: max occurrences per lane (R <= 32 * RJ).
-template <int RJ, class KeyFn, class ContFn>
+//   stop(score, prob, d, rem): checked before depth d with the score and
+//                 chain probability so far and rem = the scored depths left
+//                 (warp-uniform); true gives the candidate up (the result
+//                 then has stopped set and is not a valid expansion).
+template <int RJ, class KeyFn, class ContFn, class StopFn = NeverStop>
 __device__ ExpandResult warp_expand(KeyFn key_of, ContFn cont, int n_occ,
                                     int K, long long cap, bool stop_at_cap,
                                     float min_prob, float alpha,
-                                    const VoteScratch& vs, int* chain_out) {
+                                    const VoteScratch& vs, int* chain_out,
+                                    StopFn stop = StopFn()) {
   const int lane = lane_id();
   const unsigned lt_mask = (1u << lane) - 1u;
   int depth_end = K;
@@ -260,14 +273,23 @@ __device__ ExpandResult warp_expand(KeyFn key_of, ContFn cont, int n_occ,
   int written = 0;  // depths [0, written) of chain_out are final
   int first = 0;    // lowest alive lane when nslots == 1
   bool unanimous = false;  // the last multi-slot vote had every survivor agree
+  const int scored_end = cap < depth_end ? static_cast<int>(cap > 0 ? cap : 0)
+                                         : depth_end;
+  bool stopped = false;
   for (int d = 0; d < depth_end && n > 0; ++d) {
-    if (nslots == 1 || unanimous) {
+    if (stop(score, prob, d, scored_end > d ? scored_end - d : 0)) {
+      stopped = true;
+      break;
+    }
+    if (nslots == 1 || (unanimous && depth_end - d >= 4)) {
       // Unanimous lookahead: while every survivor has the same token, the
       // vote is that token with count = active = survivors, so the depths
       // can be committed without voting (same fp32 steps). With one slot
       // per lane it is tried at every depth; with more, only after a
-      // unanimous vote, and the first survivor (lowest slot, then lowest
-      // lane) publishes its tokens before the others compare.
+      // unanimous vote and with at least 4 depths to go (it reads 8 depths
+      // of every survivor: measured at 2-4 single-depth votes' cost), and
+      // the first survivor (lowest slot, then lowest lane) publishes its
+      // tokens before the others compare.
       const int ahead = min(8, depth_end - d);
       int r[8];
       int agree = ahead;
@@ -386,8 +408,8 @@ __device__ ExpandResult warp_expand(KeyFn key_of, ContFn cont, int n_occ,
     for (int j = 0; j < RJ; ++j)
       if (j < nslots && v[j] != best_tok) amask &= ~(1u << j);
     n = best_cnt;
-    if (nslots > 1 && n <= 32) {
-      // compact the survivors to one per lane
+    if (nslots > 1 && n <= 32 * (nslots - 1)) {
+      // compact the survivors into the fewest slots (occurrence order)
       int base = 0;
 #pragma unroll
       for (int j = 0; j < RJ; ++j) {
@@ -399,9 +421,17 @@ __device__ ExpandResult warp_expand(KeyFn key_of, ContFn cont, int n_occ,
         }
       }
       __syncwarp();
-      e[0] = lane < n ? vs.act[lane] : 0;
-      amask = lane < n ? 1u : 0u;
-      nslots = 1;
+      const int ns = (n + 31) >> 5;
+      amask = 0;
+#pragma unroll
+      for (int j = 0; j < RJ; ++j) {
+        const int i = 32 * j + lane;
+        if (j < ns) {
+          e[j] = i < n ? vs.act[i] : 0;
+          if (i < n) amask |= 1u << j;
+        }
+      }
+      nslots = ns;
       __syncwarp();
     }
     if (nslots == 1)
@@ -415,6 +445,7 @@ __device__ ExpandResult warp_expand(KeyFn key_of, ContFn cont, int n_occ,
   const long long c0 = cap > 0 ? cap : 0;
   res.emit = static_cast<int>(nv < c0 ? nv : c0);
   res.score = score;
+  res.stopped = stopped;
   return res;
 }
 

@@ -20,8 +20,8 @@ therefore collective: every rank calls them, possibly with nothing to add.
   suffix-array samples on the shard that holds them, and returns each
   row's samples to its owner (a sum reduce-scatter); the owner drafts from
   its copy of the corpus. Collectives per step: all-gather (tails),
-  all-reduce SUM (bounds), reduce-scatter (samples), and on larger jobs an
-  all-reduce MAX before the bounds (each row's longest match, so that only
+  all-reduce SUM (bounds), reduce-scatter (samples), and from 8 ranks on
+  an all-reduce MAX before the bounds (each row's longest match, so that only
   the lengths the caps select are searched). They run on a side stream
   while the local step and the delta scan of the rank's own rows run on
   the caller's.
@@ -275,7 +275,7 @@ class ShardedSuffixDrafter(ReplicatedSuffixDrafter):
         # longest match first), or "auto": longest first from
         # longest_first_from ranks on
         self.length_search = "auto"
-        self.longest_first_from = 4
+        self.longest_first_from = 8
         # a list to collect (phase, event) pairs of eager steps, or None
         self.phase_events = None
 
@@ -348,7 +348,10 @@ class ShardedSuffixDrafter(ReplicatedSuffixDrafter):
         names the stream's sequence of phases ("chain": the shard chain on
         the side stream, "own": the rank's own rows)."""
         if self.phase_events is not None:
-            ev = torch.cuda.Event(enable_timing=True)
+            # under graph capture the record becomes an event-record node
+            ev = torch.cuda.Event(
+                enable_timing=True,
+                external=torch.cuda.is_current_stream_capturing())
             ev.record()
             self.phase_events.append((lane, name, ev))
 
