@@ -29,6 +29,8 @@
 // (group, second key) and scattered back into their groups' slots.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "sg_common.cuh"
@@ -272,6 +274,167 @@ __global__ void __launch_bounds__(kScanThreads)
     if (t < m) dense[V[t]] = pre + __popc(bal & ((2u << lane) - 1u)) - 1u;
     carry = tot;
     __syncthreads();
+  }
+}
+
+// Dense token ids without sorting, when the tokens other than the PAD
+// sentinel (int32 max) span a range [lo, hi] of at most 64 n values: a
+// presence bitmap over the range, per-word prefix popcounts, and each
+// token's id = the number of distinct values below it (PAD, the largest
+// value, gets the top id). The same ids as the first-token sort gives,
+// without its four digit passes over all n suffixes.
+__global__ void range_init_kernel(int32_t* r) {
+  r[0] = INT32_MAX;  // min of the non-PAD tokens
+  r[1] = INT32_MIN;  // max of the non-PAD tokens
+  r[2] = 0;          // a PAD token occurs
+}
+
+__global__ void __launch_bounds__(256)
+    token_range_kernel(const int32_t* __restrict__ tok, int64_t n,
+                       int32_t* __restrict__ r) {
+  __shared__ int s_lo[8], s_hi[8];
+  __shared__ unsigned s_pad[8];
+  int lo = INT32_MAX, hi = INT32_MIN;
+  unsigned pad = 0;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x +
+                   threadIdx.x;
+       i < n; i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int v = tok[i];
+    if (v == INT32_MAX) {
+      pad = 1;
+    } else {
+      lo = min(lo, v);
+      hi = max(hi, v);
+    }
+  }
+  lo = __reduce_min_sync(SG_FULL_MASK, lo);
+  hi = __reduce_max_sync(SG_FULL_MASK, hi);
+  pad = __reduce_or_sync(SG_FULL_MASK, pad);
+  if (lane_id() == 0) {
+    s_lo[warp_id()] = lo;
+    s_hi[warp_id()] = hi;
+    s_pad[warp_id()] = pad;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {  // one set of atomics per block
+    for (int w = 1; w < 8; ++w) {
+      lo = min(lo, s_lo[w]);
+      hi = max(hi, s_hi[w]);
+      pad |= s_pad[w];
+    }
+    if (lo != INT32_MAX) atomicMin(&r[0], lo);
+    if (hi != INT32_MIN) atomicMax(&r[1], hi);
+    if (pad) atomicOr(&r[2], 1);
+  }
+}
+
+// Bits are set only when not yet set (frequent tokens would otherwise
+// pile atomics onto a few words); a bitmap of at most kSmemWords words is
+// built in the block's shared memory first and OR-ed out once.
+constexpr int kSmemWords = 12288;  // 48 KB
+
+__global__ void __launch_bounds__(256)
+    bitmap_set_kernel(const int32_t* __restrict__ tok, int64_t n, int64_t lo,
+                      int64_t nw, uint32_t* __restrict__ bm) {
+  __shared__ uint32_t sbm[kSmemWords];
+  const bool local = nw <= kSmemWords;
+  if (local) {
+    for (int k = threadIdx.x; k < nw; k += blockDim.x) sbm[k] = 0u;
+    __syncthreads();
+  }
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x +
+                   threadIdx.x;
+       i < n; i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int v = tok[i];
+    if (v == INT32_MAX) continue;
+    const uint64_t off = static_cast<uint64_t>(static_cast<int64_t>(v) - lo);
+    const uint32_t bit = 1u << (off & 31);
+    uint32_t* word = local ? &sbm[off >> 5] : &bm[off >> 5];
+    if (!(*reinterpret_cast<volatile uint32_t*>(word) & bit))
+      atomicOr(word, bit);
+  }
+  if (local) {
+    __syncthreads();
+    for (int k = threadIdx.x; k < nw; k += blockDim.x)
+      if (sbm[k]) atomicOr(&bm[k], sbm[k]);
+  }
+}
+
+constexpr int kWordsPerBlock = 4096;  // bitmap words per scan block
+
+// Per block of kWordsPerBlock words: the number of set bits (blk_max is
+// zeroed so that round_scan_blocks_kernel serves).
+__global__ void __launch_bounds__(256)
+    bitmap_count_kernel(const uint32_t* __restrict__ bm, int64_t W,
+                        uint32_t* __restrict__ blk_max,
+                        uint32_t* __restrict__ blk_sum) {
+  __shared__ uint32_t ss[8];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kWordsPerBlock;
+  uint32_t c = 0;
+  for (int k = threadIdx.x; k < kWordsPerBlock; k += 256) {
+    const int64_t w = base + k;
+    if (w < W) c += __popc(bm[w]);
+  }
+  c = __reduce_add_sync(SG_FULL_MASK, c);
+  if (lane_id() == 0) ss[warp_id()] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t t = 0;
+    for (int w = 0; w < 8; ++w) t += ss[w];
+    blk_max[blockIdx.x] = 0;
+    blk_sum[blockIdx.x] = t;
+  }
+}
+
+// pre[w] = set bits in the words before w (block offsets from blk_sum after
+// round_scan_blocks_kernel); thread t scans 16 consecutive words.
+__global__ void __launch_bounds__(256)
+    bitmap_prefix_kernel(const uint32_t* __restrict__ bm, int64_t W,
+                         const uint32_t* __restrict__ blk_sum,
+                         uint32_t* __restrict__ pre) {
+  __shared__ uint32_t ws[8];
+  constexpr int kPer = kWordsPerBlock / 256;
+  const int64_t w0 = static_cast<int64_t>(blockIdx.x) * kWordsPerBlock +
+                     static_cast<int64_t>(threadIdx.x) * kPer;
+  uint32_t c[kPer];
+  uint32_t mine = 0;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    c[k] = w0 + k < W ? __popc(bm[w0 + k]) : 0u;
+    mine += c[k];
+  }
+  const uint32_t inc =
+      static_cast<uint32_t>(warp_incl_scan(static_cast<int>(mine)));
+  if (lane_id() == 31) ws[warp_id()] = inc;
+  __syncthreads();
+  uint32_t run = blk_sum[blockIdx.x] + inc - mine;
+  for (int w = 0; w < warp_id(); ++w) run += ws[w];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    if (w0 + k < W) pre[w0 + k] = run;
+    run += c[k];
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    bitmap_dense_kernel(const int32_t* __restrict__ tok, int64_t n,
+                        int64_t lo, const uint32_t* __restrict__ bm,
+                        const uint32_t* __restrict__ pre,
+                        const int64_t* __restrict__ n_values,
+                        uint32_t* __restrict__ dense) {
+  const uint32_t pad_id = static_cast<uint32_t>(*n_values);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x +
+                   threadIdx.x;
+       i < n; i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int v = tok[i];
+    uint32_t id = pad_id;
+    if (v != INT32_MAX) {
+      const uint64_t off =
+          static_cast<uint64_t>(static_cast<int64_t>(v) - lo);
+      const uint64_t w = off >> 5;
+      id = pre[w] + __popc(bm[w] & ((1u << (off & 31)) - 1u));
+    }
+    dense[i] = id;
   }
 }
 
@@ -852,27 +1015,35 @@ class CountSlot {
   }
   CountSlot(const CountSlot&) = delete;
   CountSlot& operator=(const CountSlot&) = delete;
-  int64_t* get() { return ptr_ ? ptr_ : &fallback_; }
+  int64_t* get() { return ptr_ ? ptr_ : fallback_; }  // 64 bytes
 
  private:
   int idx_ = -1;
   int64_t* ptr_ = nullptr;
-  int64_t fallback_ = 0;
+  int64_t fallback_[8] = {};
 };
 
-// Reads a device count into *out (host sync), through the build's slot.
-static int read_count(const int64_t* dev, int64_t* out, CountSlot& slot,
-                      cudaStream_t st) {
+// Reads `bytes` (<= 64, one slot) of device memory into *out (host sync),
+// through the build's slot.
+static int read_small(const void* dev, void* out, size_t bytes,
+                      CountSlot& slot, cudaStream_t st) {
+  if (bytes > 64) return SG_ERR_INVALID;
   int64_t* land = slot.get();
-  cudaError_t e = cudaMemcpyAsync(land, dev, sizeof(int64_t),
-                                  cudaMemcpyDeviceToHost, st);
+  cudaError_t e = cudaMemcpyAsync(land, dev, bytes, cudaMemcpyDeviceToHost,
+                                  st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) {
     set_cuda_error(e);
     return SG_ERR_CUDA;
   }
-  *out = *land;
+  std::memcpy(out, land, bytes);
   return SG_OK;
+}
+
+// Reads a device count into *out (host sync), through the build's slot.
+static int read_count(const int64_t* dev, int64_t* out, CountSlot& slot,
+                      cudaStream_t st) {
+  return read_small(dev, out, sizeof(int64_t), slot, st);
 }
 
 // One read through a slot of its own, for callers outside a build loop.
@@ -1007,24 +1178,79 @@ extern "C" int sg_build_suffix_array(const int32_t* tokens, int64_t n,
   SaWorkspace w = carve(workspace, n);
   CountSlot slot;
 
-  // initial pass: sort by the first token
-  init_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(
-      tokens, n, w.K[0], w.V[0]);
-  int kcur = radix_sort(w, 0, n, 32, st);
+  int kcur = 0;
   int err = SG_OK;
   int64_t m = 0;
   int acur = 0;
   int rounds = 0;
+  // Dense token ids (w.rank): from a bitmap when the tokens' range allows
+  // it, else from a sort by the first token.
+  int64_t n_distinct = 0;
+  bool dense_done = false;
+  {
+    int32_t* r = reinterpret_cast<int32_t*>(w.tile_hist);
+    const unsigned grid = static_cast<unsigned>(
+        std::min<int64_t>((n + 255) / 256, 8 * static_cast<int64_t>(num_sms())));
+    range_init_kernel<<<1, 1, 0, st>>>(r);
+    token_range_kernel<<<grid, 256, 0, st>>>(tokens, n, r);
+    int32_t rng[3] = {0, 0, 0};  // min, max of the non-PAD tokens, PAD seen
+    int rc = read_small(r, rng, sizeof(rng), slot, st);
+    if (rc != SG_OK) return rc;
+    const int64_t lo = rng[0], hi = rng[1];
+    const bool pad = rng[2] != 0;
+    const int64_t range = hi >= lo ? hi - lo + 1 : 0;
+    if (range <= 64 * n && range < (int64_t(1) << 31) - 2) {
+      uint32_t* bm = reinterpret_cast<uint32_t*>(w.LK);     // <= 8n bytes
+      uint32_t* pre = reinterpret_cast<uint32_t*>(w.K[1]);  // <= 8n bytes
+      const int64_t nw = (range + 31) / 32;
+      cudaError_t e = cudaSuccess;
+      if (nw > 0) {
+        e = cudaMemsetAsync(bm, 0, static_cast<size_t>(nw) * 4, st);
+        // few blocks when each ORs a whole shared bitmap out at its end
+        const unsigned gset =
+            nw <= kSmemWords
+                ? std::min<unsigned>(grid, 2u * static_cast<unsigned>(num_sms()))
+                : grid;
+        bitmap_set_kernel<<<gset, 256, 0, st>>>(tokens, n, lo, nw, bm);
+        const int nb = static_cast<int>((nw + kWordsPerBlock - 1) /
+                                        kWordsPerBlock);
+        bitmap_count_kernel<<<nb, 256, 0, st>>>(bm, nw, w.blk_max, w.blk_sum);
+        round_scan_blocks_kernel<<<1, 1024, 0, st>>>(w.blk_max, w.blk_sum,
+                                                     nb, w.m_dev);
+        bitmap_prefix_kernel<<<nb, 256, 0, st>>>(bm, nw, w.blk_sum, pre);
+      } else {
+        e = cudaMemsetAsync(w.m_dev, 0, sizeof(int64_t), st);
+      }
+      if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return SG_ERR_CUDA;
+      }
+      bitmap_dense_kernel<<<grid, 256, 0, st>>>(tokens, n, lo, bm, pre,
+                                                w.m_dev, w.rank);
+      int64_t values = 0;
+      rc = read_count(w.m_dev, &values, slot, st);
+      if (rc != SG_OK) return rc;
+      n_distinct = values + (pad ? 1 : 0);
+      dense_done = true;
+    }
+  }
+  if (!dense_done) {
+    // initial pass: sort by the first token
+    init_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0,
+                       st>>>(tokens, n, w.K[0], w.V[0]);
+    kcur = radix_sort(w, 0, n, 32, st);
+  }
   // Two-token pass in place of the first doubling round: with the D
   // distinct tokens renumbered 0 .. D - 1 in order, a suffix's first two
   // tokens pack into 2 * bitlen(D) <= 62 bits, and one sort of all n
   // suffixes by them leaves the same groups and ranks as that round (whose
   // active list, on copy-heavy text, is most of the corpus) at the price of
   // ceil(2 * bitlen(D) / 8) digit passes.
-  int64_t n_distinct = 0;
-  int rc0 = dense_ids(w, kcur, n, slot, st, &n_distinct);
-  if (rc0 != SG_OK) return rc0;
-  if (n_distinct == n) {
+  if (!dense_done) {
+    const int rc0 = dense_ids(w, kcur, n, slot, st, &n_distinct);
+    if (rc0 != SG_OK) return rc0;
+  }
+  if (n_distinct == n && !dense_done) {
     // every first token differs: sorted already, no common prefixes
     if (!apply_round(w, kcur, nullptr, w.act[acur], n, sa_out, slot, st, &m,
                      &err))
@@ -1037,7 +1263,8 @@ extern "C" int sg_build_suffix_array(const int32_t* tokens, int64_t n,
     if (!apply_round(w, kcur, nullptr, w.act[acur], n, sa_out, slot, st, &m,
                      &err))
       return err;
-    rounds = 1;
+    // every first token distinct: no common prefixes, no doubling round
+    rounds = n_distinct == n ? 0 : 1;
   }
   const int sb = bitlen(static_cast<uint64_t>(n));        // rank[i+h]+1 <= n
   const int pb = bitlen(static_cast<uint64_t>(n - 1));    // group start < n
