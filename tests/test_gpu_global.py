@@ -63,6 +63,32 @@ def test_suffix_array_edge_tokens():
         .tolist() == [0]
 
 
+@pytest.mark.parametrize("case", ["distinct", "distinct_pad", "wide_range",
+                                  "pad_only"])
+def test_suffix_array_dense_id_paths(case):
+    """Both ways to the dense token ids (a presence bitmap when the non-PAD
+    tokens span at most 64 n values, the first-token sort otherwise) give
+    the oracle's array, and rounds = 0 exactly when every token differs."""
+    from suffixgpu_b200 import ops
+    rng = np.random.default_rng(17)
+    n = 3000
+    if case == "distinct":
+        tok = rng.permutation(n).astype(np.int32) - 7
+    elif case == "distinct_pad":
+        tok = rng.permutation(n).astype(np.int32)
+        tok[-1] = 2 ** 31 - 1
+    elif case == "wide_range":
+        tok = rng.integers(0, 50, size=n).astype(np.int32)
+        tok[::97] = rng.integers(-2 ** 31, 2 ** 31 - 2, size=tok[::97].size)
+    else:
+        tok = np.full(n, 2 ** 31 - 1, dtype=np.int32)
+    t = _dev(tok)
+    out = torch.empty(n, dtype=torch.int32, device=DEV)
+    rounds = ops.build_suffix_array_into(t, out)
+    np.testing.assert_array_equal(_host(out), so.build_suffix_array(tok))
+    assert (rounds == 0) == (np.unique(tok).size == n)
+
+
 def _sa_is_sorted(tok: np.ndarray, sa: np.ndarray) -> None:
     """Linear-time certificate that sa is the suffix array of tok: a
     permutation, and consecutive suffixes ordered by (token, rank of the
