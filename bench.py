@@ -44,7 +44,8 @@ CONFIG = {"workload": "config2: local-only propose_with_update, B=256, "
                       "S=8192, k=16, P=32, R=128, C=8, factor=2.0, "
                       "min_prob=0.1, 100-step decode loop",
           "global_batch": B, "seq_len": S,
-          "l2": "inputs larger than L2: 32 rotating replicas x 8 MiB"}
+          "l2": "inputs larger than L2: 32 rotating replicas x 8 MiB",
+          "rows_per_gpu": "the same seeded 256 rows on every GPU"}
 
 
 def parse():
@@ -99,8 +100,13 @@ def parse():
 # workload
 # ---------------------------------------------------------------------------
 def workload(rank: int):
+    """Config 2's rows and decode steps. Every rank drafts the same seeded
+    256 rows (weak scaling with identical per-GPU work: a step's time is
+    its slowest row's, so rows drawn per rank would make the max over
+    ranks measure sampling variance rather than the system)."""
     from suffixgpu_b200 import workloads as wl
-    return wl.config2(seed=2 + 1000 * rank, steps=DECODE_STEPS)
+    del rank
+    return wl.config2(seed=2, steps=DECODE_STEPS)
 
 
 def algorithmic_bytes(data, rep_shift) -> np.ndarray:
@@ -601,7 +607,8 @@ def run_sharded(args, dev, world: int, rank: int) -> dict | None:
     import torch
     from suffixgpu_b200 import workloads as wl
     lg = min(26, max(16, args.sharded_log2_corpus))
-    data = wl.config5(rank=rank, steps=DECODE5, n_docs=1 << (lg - 10))
+    # every rank drafts the same seeded 128 rows (identical per-GPU work)
+    data = wl.config5(rank=0, steps=DECODE5, n_docs=1 << (lg - 10))
     docs = torch.from_numpy(data["corpus_docs"]).to(dev)
     res = {}
     for mode in ("shards", "replicated"):
