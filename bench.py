@@ -1,4 +1,4 @@
-"""Benchmark: propose_with_update rows/s on BASELINE config 2
+"""Benchmark: propose_with_update rows/s on benchmark config 2
 (B=256, S=8192, k=16, P=32, R=128, 8 backoff candidates, factor 2.0,
 min_token_prob 0.1) on 1..8 GPUs of one node.
 
@@ -392,7 +392,7 @@ def run_ours(args):
             "scaling": "weak",
             "vs_baseline": None,
             "dtype": "int32",
-            "data": "synthetic (seeded copy/Zipf rows, BASELINE config 2)",
+            "data": "synthetic (seeded copy/Zipf rows, benchmark config 2)",
             "config": dict(CONFIG, parallelism=f"dp{world}",
                            timing=timing),
             "impl": "ours",
@@ -503,7 +503,7 @@ def run_rebuild(args, dev) -> dict:
 
 
 def run_sa(args, dev) -> dict:
-    """suffix array of 2^24 tokens (50% i.i.d. Zipf,
+    """benchmark config 4: suffix array of 2^24 tokens (50% i.i.d. Zipf,
     50% copies of earlier spans). Times whole builds with CUDA events; the
     build synchronises once per doubling round, so the time includes those
     host round trips."""
@@ -558,7 +558,7 @@ def run_sa(args, dev) -> dict:
 
 
 def run_queries(args, tok, sa, dev, peaks) -> dict:
-    """BASELINE config 4 queries: 1000 corpus substrings per capped length
+    """benchmark config 4 queries: 1000 corpus substrings per capped length
     (32, 16, 8, 4, 2) against the built SA, all 5000 in one search_interval
     launch (rows padded to width 32, pattern length per row). Every pattern
     occurs in the corpus, so every interval must be non-empty: a
@@ -610,7 +610,7 @@ NREP5, DECODE5 = 16, 32
 
 
 def run_sharded(args, dev, world: int, rank: int) -> dict | None:
-    """the global drafter on every GPU of the job, 128
+    """benchmark config 5: the global drafter on every GPU of the job, 128
     query rows (S=16384) per GPU, k=32, P=64, R=256, 8 backoff levels,
     factor 2.0, min_prob 0.1, over a 2^26-token template corpus (512
     templates x 512, vocab 128256) that every rank bulk-loads from the same
@@ -803,7 +803,7 @@ def _run_config5_mode(args, dev, world, rank, mode, data, docs, lg):
 
 
 def run_global(args, dev) -> dict:
-    """global memory enabled (capacity 2^22, delta
+    """benchmark config 3: global memory enabled (capacity 2^22, delta
     2^16, rebuild threshold 32768), corpus of 4096 template documents x
     1024 tokens pre-filled through harvest_rows, then B=64 x S=4096 query
     rows decoded step by step. Every step harvests 4 finished rows of the
@@ -1206,7 +1206,7 @@ def run_reference(args):
         "ms_per_step": 1e3 * min(args.cpu_rows, B) / v,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int32",
-        "data": "synthetic (seeded copy/Zipf rows, BASELINE config 2)",
+        "data": "synthetic (seeded copy/Zipf rows, benchmark config 2)",
         "config": dict(CONFIG, parallelism="host cores"),
         "impl": "reference", "cpu_baseline": cb,
         "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0,

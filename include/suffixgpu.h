@@ -409,7 +409,7 @@ int sg_global_draft(const int64_t* sa_len, const int64_t* sa_start,
                     const float* local_score, const uint8_t* row_mask,
                     int32_t* draft, int32_t* num_valid, sg_stream_t stream);
 
-/* ---- suffix-array shards (multi-GPU global drafter) ---
+/* ---- suffix-array shards (multi-GPU global drafter, benchmark config 5) ---
  * No reference counterpart: the reference has one suffix array on one
  * device. These calls split its query across GPUs without changing its
  * result: each GPU keeps the suffixes that start in its share of the corpus

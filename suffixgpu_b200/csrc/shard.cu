@@ -1,4 +1,4 @@
-// Suffix-array shards for the multi-GPU global drafter.
+// Suffix-array shards for the multi-GPU global drafter (benchmark config 5).
 //
 // The reference has one suffix array over the whole corpus and samples a
 // match interval in suffix-array order: with ilen suffixes in [start, end)

@@ -1,4 +1,4 @@
-"""Multi-GPU drafters for BASELINE config 5 (the 8-GPU global drafter).
+"""Multi-GPU drafters for benchmark config 5 (the 8-GPU global drafter).
 
 The reference has no multi-GPU code; its semantics are those of one
 drafter with one global index. Both drafters here keep them bit for bit,

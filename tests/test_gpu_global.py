@@ -105,7 +105,7 @@ def _sa_is_sorted(tok: np.ndarray, sa: np.ndarray) -> None:
 
 
 def test_suffix_array_config4_size_property():
-    """BASELINE config 4 at full size (2^24 tokens, 50% copies): checked by
+    """benchmark config 4 at full size (2^24 tokens, 50% copies): checked by
     the linear-time sortedness certificate."""
     from suffixgpu_b200 import ops
     from suffixgpu_b200 import workloads as wl

@@ -80,7 +80,7 @@ def test_local_random_vs_oracle(ci, shape):
 
 
 def test_config2_full_size_vs_oracle():
-    """B=256, S=8192: two decode steps bit-exact."""
+    """B=256, S=8192 (benchmark config 2): two decode steps bit-exact."""
     from suffixgpu_b200 import workloads as wl
     data = wl.config2(seed=5, steps=2)
     sc = {"drafter": dict(wl.CONFIG2_DRAFTER), "data": data,
