@@ -362,13 +362,16 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
                    a.out.new_counts + b);
 
   // ---- 2. match_back: ordered hit lists per warp segment -----------------
-  // Each warp owns a contiguous segment of 1024-token chunks. In a chunk,
-  // lane l examines the 32 tokens [32 l, 32 l + 32) as one bit mask; its 8
-  // vector loads go in a lane-rotated order, so each load instruction of the
-  // warp is free of bank conflicts. One prefix sum of the per-lane hit
-  // counts then places the positions in order.
+  // Each warp owns an equal contiguous segment (a multiple of 32 tokens),
+  // walked in 1024-token chunks. In a chunk, lane l examines the 32 tokens
+  // [32 l, 32 l + 32) as one bit mask; its 8 vector loads go in a
+  // lane-rotated order, so each load instruction of the warp is free of bank
+  // conflicts. One prefix sum of the per-lane hit counts then places the
+  // positions in order.
   const int nw = (nload + 3) >> 2;  // 4-token words
-  const int seg = ((nw + kLocalWarps - 1) / kLocalWarps + 255) & ~255;
+  // equal segments (whole 8-word lane groups) so that every warp scans a
+  // share of the row: 1024-token segments left warps idle on shorter rows
+  const int seg = ((nw + kLocalWarps - 1) / kLocalWarps + 7) & ~7;
   const int hstride = P + 2;
   int* my_ge = whist + warp * hstride;
   int* my_hits;
@@ -386,18 +389,24 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
       carry = (w_begin > 0 ? tok_s[4 * w_begin - 1] : -1) == pt0;
     for (int c0 = w_begin; c0 < w_end; c0 += 256) {
       const int wl = c0 + 8 * lane;  // this lane's first word
-      uint32_t eq = 0;               // bit q: token 4 wl + q == pat[0]
+      // The 8 loads are issued together and compared afterwards (a load
+      // under a branch waits for the compare before it); a word past the
+      // segment reads the segment's first word and is masked out.
+      int4 v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int w = wl + ((k + lane) & 7);
+        v[k] = tok4[w < w_end ? w : w_begin];
+      }
+      uint32_t eq = 0;  // bit q: token 4 wl + q == pat[0]
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const int j = (k + lane) & 7;
-        if (wl + j < w_end) {
-          const int4 v = tok4[wl + j];
-          const uint32_t bits = static_cast<uint32_t>(v.x == pt0) |
-                                (static_cast<uint32_t>(v.y == pt0) << 1) |
-                                (static_cast<uint32_t>(v.z == pt0) << 2) |
-                                (static_cast<uint32_t>(v.w == pt0) << 3);
-          eq |= bits << (4 * j);
-        }
+        const uint32_t bits = static_cast<uint32_t>(v[k].x == pt0) |
+                              (static_cast<uint32_t>(v[k].y == pt0) << 1) |
+                              (static_cast<uint32_t>(v[k].z == pt0) << 2) |
+                              (static_cast<uint32_t>(v[k].w == pt0) << 3);
+        eq |= wl + j < w_end ? bits << (4 * j) : 0u;
       }
       // end position 4 wl + p is a hit iff token 4 wl + p - 1 matches: bit
       // p - 1 of eq, or bit 31 of the previous lane's mask for p = 0
@@ -405,7 +414,9 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
       uint32_t hm = (eq << 1) | (lane == 0 ? carry : (up >> 31));
       carry = __shfl_sync(SG_FULL_MASK, eq, 31) >> 31;
       const int p0 = 4 * wl;
-      const int nvalid = nload - p0;  // positions >= nload are not ends
+      // ends at or past nload are no positions; ends at or past the
+      // segment's end belong to the next warp, which counts them by carry
+      const int nvalid = min(nload, 4 * w_end) - p0;
       if (nvalid < 32) hm &= nvalid <= 0 ? 0u : ((1u << nvalid) - 1u);
       if (__ballot_sync(SG_FULL_MASK, hm != 0) == 0) continue;
       const int c = __popc(hm);
@@ -415,49 +426,76 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
         const int x = __shfl_up_sync(SG_FULL_MASK, inc, o);
         if (lane >= o) inc += x;
       }
+      // the lane's hits in order, as many rounds as the busiest lane has
+      // (a warp-uniform loop: no divergent per-lane loop)
       int pos = nh + inc - c;
-      while (hm) {
-        const int bit = __ffs(hm) - 1;
-        hm &= hm - 1;
-        my_hits[pos++] = p0 + bit;
+      const int rounds = __reduce_max_sync(SG_FULL_MASK, c);
+      for (int r = 0; r < rounds; ++r) {
+        if (hm) {
+          my_hits[pos++] = p0 + __ffs(hm) - 1;
+          hm &= hm - 1;
+        }
       }
       nh += __shfl_sync(SG_FULL_MASK, inc, 31);
     }
     __syncwarp();
-    // 2b. extend every hit; consecutive lanes take consecutive hits
+    // 2b. extend every hit; consecutive lanes take consecutive hits, four
+    // per lane in flight (their loads go out together)
     const int pt1 = P > 1 ? pat[1] : INT32_MIN;
     const int pt2 = P > 2 ? pat[2] : INT32_MIN;
     const int pt3 = P > 3 ? pat[3] : INT32_MIN;
     int h1 = 0, h2 = 0, h3 = 0, h4 = 0, hp = 0;
-    for (int i = lane; i < nh; i += 32) {
-      const int e = my_hits[i];
-      const int t1 = e >= 2 ? tok_s[e - 2] : -1;
-      const int t2 = e >= 3 ? tok_s[e - 3] : -1;
-      const int t3 = e >= 4 ? tok_s[e - 4] : -1;
-      int m = 1;
-      if (t1 == pt1) {
-        m = 2;
-        if (t2 == pt2) {
-          m = 3;
-          if (t3 == pt3) {
-            m = 4;
-            for (int tt = 4; tt < P; ++tt) {
-              const int y = e - 1 - tt;
-              const int v = y >= 0 ? tok_s[y] : -1;
-              if (v != pat[tt]) break;
-              ++m;
+    for (int i0 = lane; i0 < nh; i0 += 128) {
+      int e[4], t1[4], t2[4], t3[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + 32 * u;
+        e[u] = i < nh ? my_hits[i] : 0;  // 0: no tokens before it
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        t1[u] = e[u] >= 2 ? tok_s[e[u] - 2] : -1;
+        t2[u] = e[u] >= 3 ? tok_s[e[u] - 3] : -1;
+        t3[u] = e[u] >= 4 ? tok_s[e[u] - 4] : -1;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + 32 * u;
+        if (i >= nh) break;
+        int m = 1;
+        if (t1[u] == pt1) {
+          m = 2;
+          if (t2[u] == pt2) {
+            m = 3;
+            if (t3[u] == pt3) {
+              m = 4;
+              // four tokens (and pattern entries) per round trip
+              for (int tt = 4; tt < P; tt += 4) {
+                int run = 0;
+                bool go = true;
+#pragma unroll
+                for (int z = 0; z < 4; ++z) {
+                  const int y = e[u] - 1 - tt - z;
+                  const int x = y >= 0 ? tok_s[y] : -1;
+                  const int pv = pat[min(tt + z, P - 1)];
+                  go = go && tt + z < P && x == pv;
+                  run += go;
+                }
+                m += run;
+                if (run < 4) break;
+              }
             }
           }
         }
+        if (m > P) m = P;
+        h1 += m == 1;
+        h2 += m == 2;
+        h3 += m == 3;
+        h4 += m == 4;
+        hp += m == P && P > 4;  // full-length matches: no atomic per hit
+        if (m > 4 && m < P) atomicAdd(&my_ge[m], 1);
+        my_hits[i] = (e[u] << 8) | m;
       }
-      if (m > P) m = P;
-      h1 += m == 1;
-      h2 += m == 2;
-      h3 += m == 3;
-      h4 += m == 4;
-      hp += m == P && P > 4;  // full-length matches: no atomic per hit
-      if (m > 4 && m < P) atomicAdd(&my_ge[m], 1);
-      my_hits[i] = (e << 8) | m;
     }
     h1 = warp_sum(h1);
     h2 = warp_sum(h2);
