@@ -293,7 +293,7 @@ struct GlobalDraftLayout {
 };
 
 template <int RJ>
-__global__ void __launch_bounds__(kGThreads)
+__global__ void __launch_bounds__(kGThreads, 1)
     global_draft_kernel(const GlobalDraftArgs d) {
   extern __shared__ __align__(16) unsigned char gsm[];
   const GlobalCandArgs& a = d.g;

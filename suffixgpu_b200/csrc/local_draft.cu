@@ -610,7 +610,9 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
     auto key_of = [&](int i) -> int { return oc[i]; };
     auto cont = [&](int e, int d) -> int {
       const int x = e + d;  // e < S < 2^23, d < 64
-      return x < q32 ? tok_s[x < S ? x : S - 1] : -1;
+      // the load is unconditional (an address in the row), the mask after
+      const int v = tok_s[x < S ? x : S - 1];
+      return x < q32 ? v : -1;
     };
     // The selection (step 4) takes the first maximum of score + f32(cand)
     // * 1e-6. With alpha >= 0 a depth's ratio count / (active + alpha) is

@@ -9,21 +9,24 @@
 // valid while the count is positive and the probability >= min_token_prob;
 // the score sums the probabilities of valid depths below the cap.
 //
-// B200 design: one warp per candidate, survivors resident in registers.
-// Instead of sorting the R values of every depth (the Triton kernel) or
-// comparing all pairs (the torch path), each lane holds up to RJ
-// occurrences and an alive bit per slot; a depth reads one token per alive
-// slot and votes:
-//   * <= 32 survivors (one per lane): each lane counts its token among the
-//     32 in a shared buffer (8 vector loads), then two warp reductions;
-//   * more: the median voter's token is counted with ballots and wins on a
-//     strict majority; otherwise the other tokens go through a per-warp
-//     open-addressing table in shared memory, one CAS insert + one atomic
-//     add per token, all of a lane's in flight together; every lane then
-//     empties the slots it used.
+// B200 design: one warp per candidate, survivors resident in registers
+// (each lane holds up to RJ occurrences and an alive bit per slot). The
+// cost of a depth is its chain of dependent warp operations, so the
+// expansion works in passes of up to LA depths:
+//   * every survivor reads its next LA tokens at once and measures how long
+//     it agrees with the median survivor (the leader); two packed warp sums
+//     per two depths give the leader's count and the voters at each depth,
+//     and every leading depth where the leader's token holds a strict
+//     majority is decided without counting any other token;
+//   * a depth without one gets a full vote: <= 32 survivors (one per lane)
+//     count their tokens among the 32 in a shared buffer; more survivors
+//     count the first and the last pending voter's tokens with ballots
+//     (twice at most, stopping once the uncounted votes cannot reach the
+//     best count), and only the remainder goes through a per-warp
+//     open-addressing table in shared memory (one CAS insert + one atomic
+//     add per token).
 // The winner's non-matching occurrences drop their alive bit; whenever the
-// survivors fit fewer slots they are compacted (one per lane at <= 32). While all survivors agree, up
-// to 8 depths are committed at once from a shared lookahead.
+// survivors fit fewer slots they are compacted (one per lane at <= 32).
 #pragma once
 
 #include "sg_common.cuh"
@@ -96,35 +99,43 @@ __device__ __forceinline__ void vote_small(int v, int* buf, int& best_cnt,
 }
 
 // Plurality vote over RJ slots per lane (-1 = no vote) with the hash table:
-// every token is inserted on its own (all of a lane's inserts in flight
-// together) and counted with one shared-memory atomic.
+// every token is inserted on its own and counted with one shared-memory
+// atomic. The probe loop is warp-uniform and every slot issues its atomics
+// unconditionally (an atomic under a lane condition waits for the one
+// before it): a slot with nothing to insert compares -1 against -1, or
+// adds 0, at an address of its own, which changes nothing in any order.
 template <int RJ>
 __device__ __forceinline__ void vote_hash(const int (&v)[RJ], int nslots,
                                           const VoteScratch& vs,
                                           int& best_cnt, int& best_tok,
                                           int& n_act) {
+  const int lane = lane_id();
   int hh[RJ], got[RJ];
   unsigned pend = 0;
   int mine = 0;
 #pragma unroll
   for (int j = 0; j < RJ; ++j) {
+    const bool act = j < nslots && v[j] != -1;
     got[j] = -1;
-    hh[j] = 0;
-    if (j < nslots && v[j] != -1) {
+    hh[j] = act ? static_cast<int>((static_cast<uint32_t>(v[j]) * 0x9E3779B1u) >>
+                                   vs.hshift)
+                : ((lane * RJ + j) & vs.hmask);
+    if (act) {
       pend |= 1u << j;
       ++mine;
-      hh[j] = static_cast<int>((static_cast<uint32_t>(v[j]) * 0x9E3779B1u) >>
-                               vs.hshift);
     }
   }
-  for (int probe = 0; pend && probe <= vs.hmask; ++probe) {
+  for (int probe = 0; probe <= vs.hmask; ++probe) {
+    if (!__any_sync(SG_FULL_MASK, pend != 0u)) break;
     int old[RJ];
 #pragma unroll
-    for (int j = 0; j < RJ; ++j)
-      if (pend & (1u << j)) old[j] = atomicCAS(&vs.hkey[hh[j]], -1, v[j]);
+    for (int j = 0; j < RJ; ++j) {
+      const bool p = (pend >> j) & 1u;
+      old[j] = atomicCAS(&vs.hkey[hh[j]], -1, p ? v[j] : -1);
+    }
 #pragma unroll
     for (int j = 0; j < RJ; ++j) {
-      if (pend & (1u << j)) {
+      if ((pend >> j) & 1u) {
         if (old[j] == -1 || old[j] == v[j]) {
           got[j] = hh[j];
           pend &= ~(1u << j);
@@ -136,17 +147,15 @@ __device__ __forceinline__ void vote_hash(const int (&v)[RJ], int nslots,
   }
 #pragma unroll
   for (int j = 0; j < RJ; ++j)
-    if (got[j] >= 0) atomicAdd(&vs.hcnt[got[j]], 1);
+    atomicAdd(&vs.hcnt[got[j] >= 0 ? got[j] : hh[j]], got[j] >= 0 ? 1 : 0);
   __syncwarp();
   int my_cnt = 0, my_tok = INT32_MAX;
 #pragma unroll
   for (int j = 0; j < RJ; ++j) {
-    if (got[j] >= 0) {
-      const int c = vs.hcnt[got[j]];
-      if (c > my_cnt || (c == my_cnt && v[j] < my_tok)) {
-        my_cnt = c;
-        my_tok = v[j];
-      }
+    const int c = vs.hcnt[got[j] >= 0 ? got[j] : hh[j]];
+    if (got[j] >= 0 && (c > my_cnt || (c == my_cnt && v[j] < my_tok))) {
+      my_cnt = c;
+      my_tok = v[j];
     }
   }
   n_act = __reduce_add_sync(SG_FULL_MASK, mine);
@@ -162,67 +171,171 @@ __device__ __forceinline__ void vote_hash(const int (&v)[RJ], int nslots,
   __syncwarp();
 }
 
-// Plurality vote over RJ slots per lane. The token of the median voter (in
-// occurrence order) is the leader and is counted with ballots; a strict
-// majority wins outright. Only otherwise do the remaining tokens go
-// through the hash table, with the leader's tokens left out: copies make
-// one continuation dominate, and inserting 32 equal keys serialises the
-// table's atomics on one slot. The median, not the first voter: suffix-
-// array samples come in lexicographic order, so the survivors' tokens at
-// a depth are sorted and a majority token always covers the middle.
+// The median alive survivor (occurrence order): its slot and lane. n is the
+// number of alive survivors. Suffix-array samples come in lexicographic
+// order, so a majority continuation always covers the median.
 template <int RJ>
-__device__ __forceinline__ void vote_multi(const int (&v)[RJ], int nslots,
-                                           const VoteScratch& vs,
-                                           int& best_cnt, int& best_tok,
-                                           int& n_act) {
+__device__ __forceinline__ void median_alive(unsigned amask, int n, int& slot,
+                                             int& src) {
   const unsigned lt_mask = (1u << lane_id()) - 1u;
-  unsigned bal[RJ];
-  int na = 0;
+  const int target = n >> 1;  // 0-based rank
+  // (ballots of slots past the survivors are 0: no alive bit there)
+  int before = 0, sb = 0;
+  unsigned bs = 0u;
+  slot = 0;
 #pragma unroll
   for (int j = 0; j < RJ; ++j) {
-    bal[j] = j < nslots ? __ballot_sync(SG_FULL_MASK, v[j] != -1) : 0u;
-    na += __popc(bal[j]);
-  }
-  n_act = na;
-  if (na == 0) {
-    best_cnt = 0;
-    best_tok = INT32_MAX;
-    return;
-  }
-  const int target = na >> 1;  // 0-based rank of the median voter
-  int ref = -1, before = 0;
-#pragma unroll
-  for (int j = 0; j < RJ; ++j) {
-    const int cj = __popc(bal[j]);
-    if (ref == -1 && before + cj > target) {
-      const bool me = ((bal[j] >> lane_id()) & 1u) &&
-                      __popc(bal[j] & lt_mask) == target - before;
-      const unsigned sel = __ballot_sync(SG_FULL_MASK, me);
-      ref = __shfl_sync(SG_FULL_MASK, v[j], __ffs(sel) - 1);
-    }
+    const unsigned bal = __ballot_sync(SG_FULL_MASK, (amask >> j) & 1u);
+    const int cj = __popc(bal);
+    const bool pick = before <= target && target < before + cj;
+    slot = pick ? j : slot;
+    bs = pick ? bal : bs;
+    sb = pick ? before : sb;
     before += cj;
   }
-  int cr = 0;
+  const bool me =
+      ((bs >> lane_id()) & 1u) && __popc(bs & lt_mask) == target - sb;
+  src = __ffs(__ballot_sync(SG_FULL_MASK, me)) - 1;
+}
+
+// Plurality over RJ slots per lane when the leader's token ref (count cr,
+// na voters in all) has no strict majority. One round counts the tokens
+// of the first and the last pending voter with ballots; the vote is over
+// once the uncounted votes cannot reach the best count. Copies make a few
+// continuations dominate, so this often decides it; otherwise the hash
+// table sees the rest, without the dominant keys (inserting many equal
+// keys would serialise its atomics on one slot).
+template <int RJ>
+__device__ __forceinline__ void vote_rest(const int (&v)[RJ], int nslots,
+                                          const VoteScratch& vs, int ref,
+                                          int cr, int na, int& best_cnt,
+                                          int& best_tok) {
+  best_cnt = ref != -1 ? cr : 0;
+  best_tok = best_cnt > 0 ? ref : INT32_MAX;
+  int rem = na - best_cnt;  // votes not yet counted
+  unsigned pend = 0u;
 #pragma unroll
   for (int j = 0; j < RJ; ++j)
-    if (j < nslots) cr += __popc(__ballot_sync(SG_FULL_MASK, v[j] == ref));
-  if (2 * cr > na) {
-    best_cnt = cr;
-    best_tok = ref;
-    return;
+    if (j < nslots && v[j] != -1 && v[j] != ref) pend |= 1u << j;
+  {  // one round
+    if (rem < best_cnt || rem == 0) return;
+    unsigned bal[RJ];  // (pending bits are never past nslots)
+#pragma unroll
+    for (int j = 0; j < RJ; ++j)
+      bal[j] = __ballot_sync(SG_FULL_MASK, (pend >> j) & 1u);
+    int j1 = -1, l1 = 0, j2 = -1, l2 = 0;
+#pragma unroll
+    for (int j = 0; j < RJ; ++j) {
+      if (j1 < 0 && bal[j]) {
+        j1 = j;
+        l1 = __ffs(bal[j]) - 1;
+      }
+      const int jj = RJ - 1 - j;
+      if (j2 < 0 && bal[jj]) {
+        j2 = jj;
+        l2 = 31 - __clz(bal[jj]);
+      }
+    }
+    int x1 = v[0], x2 = v[0];
+#pragma unroll
+    for (int j = 1; j < RJ; ++j) {
+      if (j == j1) x1 = v[j];
+      if (j == j2) x2 = v[j];
+    }
+    const int t1 = __shfl_sync(SG_FULL_MASK, x1, l1);
+    const int t2 = __shfl_sync(SG_FULL_MASK, x2, l2);
+    int c1 = 0, c2 = 0;
+#pragma unroll
+    for (int j = 0; j < RJ; ++j) {
+      const bool p = (pend >> j) & 1u;
+      c1 += __popc(__ballot_sync(SG_FULL_MASK, p && v[j] == t1));
+      c2 += __popc(__ballot_sync(SG_FULL_MASK, p && v[j] == t2 && t2 != t1));
+    }
+    if (c1 > best_cnt || (c1 == best_cnt && t1 < best_tok)) {
+      best_cnt = c1;
+      best_tok = t1;
+    }
+    if (c2 > best_cnt || (c2 == best_cnt && c2 > 0 && t2 < best_tok)) {
+      best_cnt = c2;
+      best_tok = t2;
+    }
+#pragma unroll
+    for (int j = 0; j < RJ; ++j)
+      if (v[j] == t1 || v[j] == t2) pend &= ~(1u << j);
+    rem -= c1 + c2;
   }
+  if (rem < best_cnt || rem == 0) return;
   int w[RJ];
 #pragma unroll
-  for (int j = 0; j < RJ; ++j) w[j] = v[j] == ref ? -1 : v[j];
+  for (int j = 0; j < RJ; ++j) w[j] = ((pend >> j) & 1u) ? v[j] : -1;
   int hc, ht, hn;
   vote_hash<RJ>(w, nslots, vs, hc, ht, hn);
-  if (hc > cr || (hc == cr && ht < ref)) {
+  if (hc > best_cnt || (hc == best_cnt && hc > 0 && ht < best_tok)) {
     best_cnt = hc;
     best_tok = ht;
-  } else {
-    best_cnt = cr;
-    best_tok = ref;
   }
+}
+
+// Running state of one chain expansion.
+struct ChainState {
+  float prob;   // chain probability so far
+  float score;  // sum of the valid depths' probabilities below the cap
+  int nv;       // valid depths
+  int written;  // depths [0, written) of the chain are final
+};
+
+// The fp32 ratio count / (max(voters, 1) + alpha) of a depth, correctly
+// rounded, without contraction (with alpha 0 a count divided by itself is
+// exactly 1, as the reference's division gives).
+__device__ __forceinline__ float depth_ratio(int cnt, int act, float alpha) {
+  const float denom = __fadd_rn(static_cast<float>(act > 1 ? act : 1), alpha);
+  return __fdiv_rn(static_cast<float>(cnt), denom);
+}
+
+// Commit depth d with its count, ratio and token. False ends the chain.
+__device__ __forceinline__ bool commit_ratio(ChainState& cs, int d, int cnt,
+                                             float ratio, int tok,
+                                             float min_prob, long long cap,
+                                             int* chain_out) {
+  cs.prob = __fmul_rn(cs.prob, ratio);
+  const bool valid = cnt > 0 && cs.prob >= min_prob;
+  if (lane_id() == 0) chain_out[d] = valid ? tok : -1;
+  cs.written = d + 1;
+  if (!valid) return false;
+  ++cs.nv;
+  if (static_cast<long long>(d) < cap) cs.score = __fadd_rn(cs.score, cs.prob);
+  return true;
+}
+
+// Survivors into the fewest slots (occurrence order) once n fits in fewer.
+template <int RJ>
+__device__ __forceinline__ void compact_survivors(int (&e)[RJ], unsigned& amask,
+                                                  int& nslots, int n,
+                                                  const VoteScratch& vs) {
+  if (!(nslots > 1 && n <= 32 * (nslots - 1))) return;
+  const int lane = lane_id();
+  const unsigned lt_mask = (1u << lane) - 1u;
+  int base = 0;
+#pragma unroll
+  for (int j = 0; j < RJ; ++j) {
+    const bool alive = (amask >> j) & 1u;  // never past nslots
+    const unsigned bal = __ballot_sync(SG_FULL_MASK, alive);
+    if (alive) vs.act[base + __popc(bal & lt_mask)] = e[j];
+    base += __popc(bal);
+  }
+  __syncwarp();
+  const int ns = (n + 31) >> 5;
+  amask = 0;
+#pragma unroll
+  for (int j = 0; j < RJ; ++j) {
+    const int i = 32 * j + lane;
+    if (j < ns) {
+      e[j] = i < n ? vs.act[i] : 0;
+      if (i < n) amask |= 1u << j;
+    }
+  }
+  nslots = ns;
+  __syncwarp();
 }
 
 // Expand one candidate with the calling (full) warp.
@@ -235,18 +348,28 @@ __device__ __forceinline__ void vote_multi(const int (&v)[RJ], int nslots,
 //                operator, which also returns num_valid, does not.
 //   chain_out: K ints; entries past the last computed depth are -1.
 // RJ: max occurrences per lane (R <= 32 * RJ).
-//   stop(score, prob, d, rem): checked before depth d with the score and
-//                 chain probability so far and rem = the scored depths left
-//                 (warp-uniform); true gives the candidate up (the result
-//                 then has stopped set and is not a valid expansion).
+//   stop(score, prob, d, rem): checked before a pass of depths starting at
+//                 d with the score and chain probability so far and rem =
+//                 the scored depths left (warp-uniform); true gives the
+//                 candidate up (the result then has stopped set and is not
+//                 a valid expansion).
+//
+// A pass reads the next LA depths of every survivor at once and compares
+// them with the median survivor's (the leader's). A survivor's agreement
+// length lcp says at which depths it still votes for the leader's token, so
+// two packed warp sums give, for every depth k of the pass, the leader's
+// count c_k and the voters a_k (survivors that agreed up to k and have a
+// token there). Every leading depth with a strict majority (2 c_k > a_k) is
+// the vote's result without counting any other token; the first depth
+// without one gets a full vote (vote_small, or vote_rest knowing c_k).
 template <int RJ, class KeyFn, class ContFn, class StopFn = NeverStop>
 __device__ ExpandResult warp_expand(KeyFn key_of, ContFn cont, int n_occ,
                                     int K, long long cap, bool stop_at_cap,
                                     float min_prob, float alpha,
                                     const VoteScratch& vs, int* chain_out,
                                     StopFn stop = StopFn()) {
+  constexpr int LA = RJ <= 4 ? 4 : 1;  // depths per pass (registers)
   const int lane = lane_id();
-  const unsigned lt_mask = (1u << lane) - 1u;
   int depth_end = K;
   if (stop_at_cap)
     depth_end = cap < K ? static_cast<int>(cap > 0 ? cap : 0) : K;
@@ -264,187 +387,197 @@ __device__ ExpandResult warp_expand(KeyFn key_of, ContFn cont, int n_occ,
   }
   int n = n_occ;               // survivors (warp-uniform)
   int nslots = (n + 31) >> 5;  // slots that may hold survivors
-  const bool unit_alpha = alpha == 0.0f;
-  int* ref = vs.act + 32;      // lookahead tokens of the first survivor
 
-  float prob = 1.0f;
-  float score = 0.0f;
-  int nv = 0;
-  int written = 0;  // depths [0, written) of chain_out are final
-  int first = 0;    // lowest alive lane when nslots == 1
-  bool unanimous = false;  // the last multi-slot vote had every survivor agree
+  ChainState cs{1.0f, 0.0f, 0, 0};
   const int scored_end = cap < depth_end ? static_cast<int>(cap > 0 ? cap : 0)
                                          : depth_end;
   bool stopped = false;
-  for (int d = 0; d < depth_end && n > 0; ++d) {
-    if (stop(score, prob, d, scored_end > d ? scored_end - d : 0)) {
+  bool ended = false;  // a depth failed: the chain ends there
+
+  int d = 0;
+  while (d < depth_end && n > 0) {
+    if (stop(cs.score, cs.prob, d, scored_end > d ? scored_end - d : 0)) {
       stopped = true;
       break;
     }
-    if (nslots == 1 || (unanimous && depth_end - d >= 4)) {
-      // Unanimous lookahead: while every survivor has the same token, the
-      // vote is that token with count = active = survivors, so the depths
-      // can be committed without voting (same fp32 steps). With one slot
-      // per lane it is tried at every depth; with more, only after a
-      // unanimous vote and with at least 4 depths to go (it reads 8 depths
-      // of every survivor: measured at 2-4 single-depth votes' cost), and
-      // the first survivor (lowest slot, then lowest lane) publishes its
-      // tokens before the others compare.
-      const int ahead = min(8, depth_end - d);
-      int r[8];
-      int agree = ahead;
-      if (nslots == 1) {
-        const bool alive = amask & 1u;
-        int tk[8];
+    // ---- pass: the leader's tokens at depths d .. d + la - 1
+    int ls, ll;
+    median_alive<RJ>(amask, n, ls, ll);
+    const int la = depth_end - d < LA ? depth_end - d : LA;
+    // Every slot's LA tokens are read unconditionally (keys are always
+    // valid, the depth is clamped below depth_end) and masked afterwards: a
+    // load under a condition waits for the one before it.
+    int tk[RJ][LA];
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-          tk[u] = (u < ahead && alive) ? cont(e[0], d + u) : -1;
-        if (lane == first) {
+    for (int j = 0; j < RJ; ++j)
 #pragma unroll
-          for (int u = 0; u < 8; ++u) ref[u] = tk[u];
-        }
-        __syncwarp();
-#pragma unroll
-        for (int u = 7; u >= 0; --u) {
-          r[u] = ref[u];
-          if (u < ahead && (r[u] == -1 || (alive && tk[u] != r[u]))) agree = u;
-        }
-      } else {
-        int l0 = -1, ej = 0;
-#pragma unroll
-        for (int j = 0; j < RJ; ++j) {
-          if (j < nslots) {
-            const unsigned bal = __ballot_sync(SG_FULL_MASK, (amask >> j) & 1u);
-            if (l0 < 0 && bal) {
-              l0 = __ffs(bal) - 1;
-              ej = e[j];
-            }
-          }
-        }
-        if (lane == l0) {
-#pragma unroll
-          for (int u = 0; u < 8; ++u) ref[u] = u < ahead ? cont(ej, d + u) : -1;
-        }
-        __syncwarp();
-#pragma unroll
-        for (int u = 7; u >= 0; --u) {
-          r[u] = ref[u];
-          if (u < ahead && r[u] == -1) agree = u;
-        }
-#pragma unroll
-        for (int j = 0; j < RJ; ++j) {
-          if (j < nslots && ((amask >> j) & 1u)) {
-            int aj = agree;
-#pragma unroll
-            for (int u = 7; u >= 0; --u)
-              if (u < agree && cont(e[j], d + u) != r[u]) aj = u;
-            agree = aj < agree ? aj : agree;
-          }
-        }
-      }
-      const int run = __reduce_min_sync(SG_FULL_MASK, agree);
-      if (run > 0) {
-        const float ratio = unit_alpha
-            ? 1.0f
-            : __fdiv_rn(static_cast<float>(n),
-                        __fadd_rn(static_cast<float>(n), alpha));
-        bool stop = false;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          if (u < run && !stop) {
-            prob = __fmul_rn(prob, ratio);
-            const bool valid = prob >= min_prob;
-            if (lane == 0) chain_out[d + u] = valid ? r[u] : -1;
-            written = d + u + 1;
-            if (!valid) {
-              stop = true;
-            } else {
-              ++nv;
-              if (static_cast<long long>(d + u) < cap)
-                score = __fadd_rn(score, prob);
-            }
-          }
-        }
-        __syncwarp();
-        if (stop) break;
-        if (run < ahead) unanimous = false;  // depth d + run disagrees
-        d += run - 1;  // the loop's ++d moves to the first undecided depth
-        continue;
-      }
-      __syncwarp();
-    }
-    int v[RJ];
+      for (int u = 0; u < LA; ++u)
+        tk[j][u] = cont(e[j], u < la ? d + u : d);
 #pragma unroll
     for (int j = 0; j < RJ; ++j) {
-      v[j] = -1;
-      if (j < nslots && (amask & (1u << j))) v[j] = cont(e[j], d);
+      const bool alive = j < nslots && ((amask >> j) & 1u);
+#pragma unroll
+      for (int u = 0; u < LA; ++u)
+        if (!alive || u >= la) tk[j][u] = -1;
     }
-    int best_cnt = 0, best_tok = -1, n_act = 0;
+    // the leader's token at depth d and its count there (one packed warp
+    // sum): the rest of the pass only runs when it holds a strict majority
+    int x0 = tk[0][0];
+#pragma unroll
+    for (int j = 1; j < RJ; ++j)
+      if (j == ls) x0 = tk[j][0];
+    const int r0 = __shfl_sync(SG_FULL_MASK, x0, ll);
+    unsigned pk = 0u;
+#pragma unroll
+    for (int j = 0; j < RJ; ++j)
+      pk += (tk[j][0] != -1 ? 0x10000u : 0u) +
+            (r0 != -1 && tk[j][0] == r0 ? 1u : 0u);
+    pk = __reduce_add_sync(SG_FULL_MASK, pk);
+    int ref = r0, cr = static_cast<int>(pk & 0xffffu),
+        na = static_cast<int>(pk >> 16);
+    int v[RJ];  // the survivors' tokens at the depth that gets a full vote
+#pragma unroll
+    for (int j = 0; j < RJ; ++j) v[j] = tk[j][0];
+    if (2 * cr > na) {
+      int r[LA];
+      r[0] = r0;
+#pragma unroll
+      for (int u = 1; u < LA; ++u) {
+        int x = tk[0][u];
+#pragma unroll
+        for (int j = 1; j < RJ; ++j)
+          if (j == ls) x = tk[j][u];
+        r[u] = __shfl_sync(SG_FULL_MASK, x, ll);
+      }
+      // agreement length with the leader (lcp), and whether the survivor
+      // has a token at its first disagreeing depth (it votes there): bit
+      // masks over the pass's depths, no branches
+      int lcp[RJ];
+      bool has[RJ];
+#pragma unroll
+      for (int j = 0; j < RJ; ++j) {
+        unsigned eqm = 0u, tkm = 0u;
+#pragma unroll
+        for (int u = 0; u < LA; ++u) {
+          eqm |= static_cast<unsigned>(tk[j][u] == r[u] && r[u] != -1) << u;
+          tkm |= static_cast<unsigned>(tk[j][u] != -1) << u;
+        }
+        const int m = __ffs(~eqm) - 1;  // leading agreeing depths (<= LA)
+        const bool alive = (amask >> j) & 1u;
+        lcp[j] = alive ? m : -1;
+        has[j] = alive && ((tkm >> m) & 1u);
+      }
+      // c_k = #{lcp > k}; a_k = c_k + #{lcp == k, has}: two depths per sum
+      int cnt[LA], act[LA];
+      cnt[0] = cr;
+      act[0] = na;
+#pragma unroll
+      for (int k = 1; k < LA; k += 2) {
+        unsigned pc = 0u, pa = 0u;
+#pragma unroll
+        for (int j = 0; j < RJ; ++j) {
+          const unsigned g0 = lcp[j] > k;
+          const unsigned a0 =
+              g0 | static_cast<unsigned>(lcp[j] == k && has[j]);
+          pc += g0;
+          pa += a0;
+          if (k + 1 < LA) {
+            const unsigned g1 = lcp[j] > k + 1;
+            const unsigned a1 =
+                g1 | static_cast<unsigned>(lcp[j] == k + 1 && has[j]);
+            pc += g1 << 16;
+            pa += a1 << 16;
+          }
+        }
+        pc = __reduce_add_sync(SG_FULL_MASK, pc);
+        pa = __reduce_add_sync(SG_FULL_MASK, pa);
+        cnt[k] = static_cast<int>(pc & 0xffffu);
+        act[k] = static_cast<int>(pa & 0xffffu);
+        if (k + 1 < LA) {
+          cnt[k + 1] = static_cast<int>(pc >> 16);
+          act[k + 1] = static_cast<int>(pa >> 16);
+        }
+      }
+      // Commit the leading depths the leader's token wins by majority, with
+      // the ratios of all depths computed first (the divisions overlap); at
+      // the first depth without one, keep the leader's figures and the
+      // survivors' tokens there (inside the unrolled loop: a selection by
+      // run after it would index the arrays dynamically, through local
+      // memory).
+      float ratio[LA];
+#pragma unroll
+      for (int k = 0; k < LA; ++k)
+        ratio[k] = depth_ratio(cnt[k], act[k], alpha);
+      int run = 0, nn = n;
+      bool open = true;
+#pragma unroll
+      for (int k = 0; k < LA; ++k) {
+        const bool here = open && k < la;
+        const bool maj = here && 2 * cnt[k] > act[k];
+        const float np = __fmul_rn(cs.prob, ratio[k]);
+        const bool valid = np >= min_prob;
+        if (maj) {
+          cs.prob = np;
+          if (lane == 0) chain_out[d + k] = valid ? r[k] : -1;
+          cs.written = d + k + 1;
+          const float ns = __fadd_rn(cs.score, np);
+          if (valid) {
+            ++cs.nv;
+            if (static_cast<long long>(d + k) < cap) cs.score = ns;
+          }
+          ended = !valid;
+          ++run;
+          nn = cnt[k];
+        }
+        if (here && !maj) {
+          ref = r[k];
+          cr = cnt[k];
+          na = act[k];
+#pragma unroll
+          for (int j = 0; j < RJ; ++j) v[j] = lcp[j] >= k ? tk[j][k] : -1;
+        }
+        open = maj && valid;
+      }
+      if (ended) break;
+      d += run;
+      n = nn;
+#pragma unroll
+      for (int j = 0; j < RJ; ++j)
+        if (lcp[j] < run) amask &= ~(1u << j);
+      if (run == la) {
+        compact_survivors<RJ>(e, amask, nslots, n, vs);
+        continue;
+      }
+    }
+    // ---- full vote at depth d (the leader has no strict majority), on the
+    // pass's tokens (the slots are compacted only after it)
+    int best_cnt = 0, best_tok = -1, n_act = na;
     if (nslots == 1) {
       vote_small(v[0], vs.act, best_cnt, best_tok, n_act);
     } else {
-      vote_multi<RJ>(v, nslots, vs, best_cnt, best_tok, n_act);
-      unanimous = best_cnt == n && n_act == n;
+      vote_rest<RJ>(v, nslots, vs, ref, cr, na, best_cnt, best_tok);
     }
-    // fp32 chain probability, correctly rounded, no contraction; a
-    // unanimous vote with alpha 0 divides a count by itself: exactly 1
-    float ratio;
-    if (unit_alpha && best_cnt == n_act && n_act > 0) {
-      ratio = 1.0f;
-    } else {
-      const float denom =
-          __fadd_rn(static_cast<float>(n_act > 1 ? n_act : 1), alpha);
-      ratio = __fdiv_rn(static_cast<float>(best_cnt), denom);
+    if (!commit_ratio(cs, d, best_cnt, depth_ratio(best_cnt, n_act, alpha),
+                      best_tok, min_prob, cap, chain_out)) {
+      ended = true;
+      break;
     }
-    prob = __fmul_rn(prob, ratio);
-    const bool valid = best_cnt > 0 && prob >= min_prob;
-    if (lane == 0) chain_out[d] = valid ? best_tok : -1;
-    written = d + 1;
-    if (!valid) break;
-    ++nv;
-    if (static_cast<long long>(d) < cap) score = __fadd_rn(score, prob);
     // keep the occurrences that agree with the winner: exactly best_cnt
 #pragma unroll
     for (int j = 0; j < RJ; ++j)
-      if (j < nslots && v[j] != best_tok) amask &= ~(1u << j);
+      if (v[j] != best_tok) amask &= ~(1u << j);
     n = best_cnt;
-    if (nslots > 1 && n <= 32 * (nslots - 1)) {
-      // compact the survivors into the fewest slots (occurrence order)
-      int base = 0;
-#pragma unroll
-      for (int j = 0; j < RJ; ++j) {
-        if (j < nslots) {
-          const bool alive = (amask >> j) & 1u;
-          const unsigned bal = __ballot_sync(SG_FULL_MASK, alive);
-          if (alive) vs.act[base + __popc(bal & lt_mask)] = e[j];
-          base += __popc(bal);
-        }
-      }
-      __syncwarp();
-      const int ns = (n + 31) >> 5;
-      amask = 0;
-#pragma unroll
-      for (int j = 0; j < RJ; ++j) {
-        const int i = 32 * j + lane;
-        if (j < ns) {
-          e[j] = i < n ? vs.act[i] : 0;
-          if (i < n) amask |= 1u << j;
-        }
-      }
-      nslots = ns;
-      __syncwarp();
-    }
-    if (nslots == 1)
-      first = __ffs(__ballot_sync(SG_FULL_MASK, amask & 1u)) - 1;
+    ++d;
+    compact_survivors<RJ>(e, amask, nslots, n, vs);
   }
   // depths past the last computed one
-  for (int dd = written + lane; dd < K; dd += 32) chain_out[dd] = -1;
+  for (int dd = cs.written + lane; dd < K; dd += 32) chain_out[dd] = -1;
   __syncwarp();
   ExpandResult res;
-  res.num_valid = nv;
+  res.num_valid = cs.nv;
   const long long c0 = cap > 0 ? cap : 0;
-  res.emit = static_cast<int>(nv < c0 ? nv : c0);
-  res.score = score;
+  res.emit = static_cast<int>(cs.nv < c0 ? cs.nv : c0);
+  res.score = cs.score;
   res.stopped = stopped;
   return res;
 }
