@@ -116,12 +116,13 @@ __device__ __forceinline__ int warp_candidates(const int* ge, int P, int C,
   int cand = 0;
   for (int L0 = 1; L0 <= P; L0 += 32) {
     const int L = L0 + lane;
+    // (loads from a clamped length, masked after: no load under a branch)
+    const int Lc = L <= P ? L : P;
     int v = 0;
-    if (L <= P) {
 #pragma unroll
-      for (int w = 0; w < kLocalWarps; ++w) v += ge[w * stride + L];
-      if (cge) cge[L] = v;
-    }
+    for (int w = 0; w < kLocalWarps; ++w) v += ge[w * stride + Lc];
+    if (L > P) v = 0;
+    if (cge && L <= P) cge[L] = v;
     // cand_c = #{L : cnt_ge[L] >= 2^c}: cnt_ge is non-increasing in L
     for (int c = 0; c < C; ++c) {
       const unsigned m = __ballot_sync(SG_FULL_MASK, L <= P && v >= (1 << c));
@@ -385,8 +386,10 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
     // 2a. positions i with tok[i-1] == pat[0], in order; positions before
     // the buffer start read -1
     uint32_t carry = 0;  // token before the chunk == pat[0]
-    if (w_begin < nw)
-      carry = (w_begin > 0 ? tok_s[4 * w_begin - 1] : -1) == pt0;
+    if (w_begin < nw) {
+      const int tb = tok_s[w_begin > 0 ? 4 * w_begin - 1 : 0];
+      carry = (w_begin > 0 ? tb : -1) == pt0;
+    }
     for (int c0 = w_begin; c0 < w_end; c0 += 256) {
       const int wl = c0 + 8 * lane;  // this lane's first word
       // The 8 loads are issued together and compared afterwards (a load
@@ -441,22 +444,29 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
     __syncwarp();
     // 2b. extend every hit; consecutive lanes take consecutive hits, four
     // per lane in flight (their loads go out together)
-    const int pt1 = P > 1 ? pat[1] : INT32_MIN;
-    const int pt2 = P > 2 ? pat[2] : INT32_MIN;
-    const int pt3 = P > 3 ? pat[3] : INT32_MIN;
+    const int pr1 = pat[P > 1 ? 1 : 0], pr2 = pat[P > 2 ? 2 : 0],
+              pr3 = pat[P > 3 ? 3 : 0];
+    const int pt1 = P > 1 ? pr1 : INT32_MIN;
+    const int pt2 = P > 2 ? pr2 : INT32_MIN;
+    const int pt3 = P > 3 ? pr3 : INT32_MIN;
     int h1 = 0, h2 = 0, h3 = 0, h4 = 0, hp = 0;
     for (int i0 = lane; i0 < nh; i0 += 128) {
       int e[4], t1[4], t2[4], t3[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int i = i0 + 32 * u;
-        e[u] = i < nh ? my_hits[i] : 0;  // 0: no tokens before it
+        // (a slot past nh still lies in the hits buffer: unused)
+        const int x = my_hits[i];
+        e[u] = i < nh ? x : 0;  // 0: no tokens before it
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        t1[u] = e[u] >= 2 ? tok_s[e[u] - 2] : -1;
-        t2[u] = e[u] >= 3 ? tok_s[e[u] - 3] : -1;
-        t3[u] = e[u] >= 4 ? tok_s[e[u] - 4] : -1;
+        const int a1 = tok_s[e[u] >= 2 ? e[u] - 2 : 0];
+        const int a2 = tok_s[e[u] >= 3 ? e[u] - 3 : 0];
+        const int a3 = tok_s[e[u] >= 4 ? e[u] - 4 : 0];
+        t1[u] = e[u] >= 2 ? a1 : -1;
+        t2[u] = e[u] >= 3 ? a2 : -1;
+        t3[u] = e[u] >= 4 ? a3 : -1;
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
@@ -476,7 +486,8 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
 #pragma unroll
                 for (int z = 0; z < 4; ++z) {
                   const int y = e[u] - 1 - tt - z;
-                  const int x = y >= 0 ? tok_s[y] : -1;
+                  const int xv = tok_s[y >= 0 ? y : 0];
+                  const int x = y >= 0 ? xv : -1;
                   const int pv = pat[min(tt + z, P - 1)];
                   go = go && tt + z < P && x == pv;
                   run += go;
@@ -557,7 +568,8 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
         int got = 0;
         for (int i0 = 0; i0 < nh && got < k && got < room; i0 += 32) {
           const int i = i0 + lane;
-          const int e = i < nh ? my_hits[i] : 0;
+          const int ex = my_hits[i];  // past nh: in the buffer, unused
+          const int e = i < nh ? ex : 0;
           const bool hit = i < nh && (e & 0xff) >= cand;
           const unsigned bal = __ballot_sync(SG_FULL_MASK, hit);
           const int r = got + __popc(bal & lt_mask);
@@ -593,7 +605,8 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
         const int len = wlen[w];
         const int stop = n + kw;
         for (int i0 = 0; i0 < len && n < stop && n < R; i0 += 32) {
-          const int e = i0 + lane < len ? lst[i0 + lane] : 0;
+          const int ex = lst[i0 + lane];  // past len: in the buffer, unused
+          const int e = i0 + lane < len ? ex : 0;
           const bool hit = (e & 0xff) >= cand;
           const unsigned bal = __ballot_sync(SG_FULL_MASK, hit);
           const int r = n + __popc(bal & lt_mask);

@@ -379,11 +379,10 @@ __device__ ExpandResult warp_expand(KeyFn key_of, ContFn cont, int n_occ,
 #pragma unroll
   for (int j = 0; j < RJ; ++j) {
     const int i = j * 32 + lane;
-    e[j] = 0;
-    if (i < n_occ) {
-      e[j] = key_of(i);
-      amask |= 1u << j;
-    }
+    // the first key stands in past n_occ (read unconditionally, unused)
+    e[j] = key_of(i < n_occ ? i : 0);
+    if (i < n_occ) amask |= 1u << j;
+    else e[j] = 0;
   }
   int n = n_occ;               // survivors (warp-uniform)
   int nslots = (n + 31) >> 5;  // slots that may hold survivors
