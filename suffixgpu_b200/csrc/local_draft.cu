@@ -429,15 +429,15 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
         const int x = __shfl_up_sync(SG_FULL_MASK, inc, o);
         if (lane >= o) inc += x;
       }
-      // the lane's hits in order, as many rounds as the busiest lane has
-      // (a warp-uniform loop: no divergent per-lane loop)
+      // the lane's hits in order: a walk over the 32 bits with predicated
+      // stores (full-rate integer operations only; finding set bits one by
+      // one costs a slow-unit __ffs per hit)
       int pos = nh + inc - c;
-      const int rounds = __reduce_max_sync(SG_FULL_MASK, c);
-      for (int r = 0; r < rounds; ++r) {
-        if (hm) {
-          my_hits[pos++] = p0 + __ffs(hm) - 1;
-          hm &= hm - 1;
-        }
+#pragma unroll
+      for (int q = 0; q < 32; ++q) {
+        const unsigned bit = (hm >> q) & 1u;
+        if (bit) my_hits[pos] = p0 + q;
+        pos += bit;
       }
       nh += __shfl_sync(SG_FULL_MASK, inc, 31);
     }
