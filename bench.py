@@ -802,6 +802,68 @@ def _run_config5_mode(args, dev, world, rank, mode, data, docs, lg):
     return out
 
 
+def _global_graph_loop(args, setup, data, samp, q_host, dev) -> dict:
+    """The config-3 loop again on a fresh drafter, with propose_with_update
+    captured once into a CUDA graph (static count and sampled-id buffers,
+    the new counts written back into the count buffer) and replayed every
+    step between the harvests and the poll: the host then issues one graph
+    launch and one small copy per propose. Step 0 runs eagerly on the
+    capture stream (it creates the side streams and buffers); the timed
+    steps are the same as the eager loop's."""
+    import torch
+    d, gi, _ = setup()
+    tok = torch.from_numpy(data["token_ids"]).to(dev)
+    n = torch.from_numpy(data["num_tokens"]).to(dev)
+    b = tok.shape[0]
+    steps = args.global_warmup + args.global_steps
+    warm = max(1, args.global_warmup)
+    cap = torch.cuda.Stream(dev)
+
+    def harvest(j):
+        rows = [(4 * j + i) % b for i in range(4)]
+        d.harvest_finished(rows, [q_host[r] for r in rows], tok)
+        d.poll()
+
+    harvest(0)
+    cap.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(cap):
+        _, _, n = d.propose_with_update(n, tok, samp[0])
+    torch.cuda.synchronize()
+    n_s = n.clone()
+    samp_s = samp[0].clone()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=cap):
+        _, _, g_n = d.propose_with_update(n_s, tok, samp_s)
+        n_s.copy_(g_n)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    r0 = gi.rebuilds
+    t1 = time.perf_counter()
+    for j in range(1, steps):
+        if j == warm:
+            torch.cuda.synchronize()
+            r0 = gi.rebuilds
+            t1 = time.perf_counter()
+            e0.record()
+        harvest(j)
+        samp_s.copy_(samp[j])
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t1
+    timed = steps - warm
+    ms = e0.elapsed_time(e1) / timed
+    rebuilds = gi.rebuilds - r0
+    gi.wait_rebuild()
+    del graph
+    return {"value": b / (ms * 1e-3), "unit": "rows/s", "ms_per_step": ms,
+            "wall_ms_per_step": wall * 1e3 / timed, "steps": timed,
+            "rebuilds_in_timed_steps": rebuilds,
+            "mode": "same loop, propose_with_update replayed from one CUDA "
+                    "graph (harvests, polls and background rebuilds "
+                    "eager)"}
+
+
 def run_global(args, dev) -> dict:
     """benchmark config 3: global memory enabled (capacity 2^22, delta
     2^16, rebuild threshold 32768), corpus of 4096 template documents x
@@ -817,23 +879,30 @@ def run_global(args, dev) -> dict:
     steps = args.global_warmup + args.global_steps
     data = wl.config3(seed=3, steps=steps)
     b, s = data["token_ids"].shape
-    d = SuffixGPUDrafter(k=16, device=dev, max_pattern_len=32,
-                         max_occurrences=128, num_backoff=8,
-                         enable_global=True, global_capacity=1 << 22,
-                         delta_capacity=1 << 16, rebuild_threshold=32768,
-                         rebuild_stream=torch.cuda.Stream(dev))
-    gi = d.global_index
     docs = torch.from_numpy(data["corpus_docs"]).to(dev)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    per = 16
-    for i in range(0, docs.shape[0], per):
-        d.harvest_rows([docs[j] for j in range(i, min(i + per, docs.shape[0]))],
-                       [docs.shape[1]] * min(per, docs.shape[0] - i))
-        gi.wait_rebuild()  # no document dropped while pre-filling
-    gi.wait_rebuild()
-    torch.cuda.synchronize()
-    prefill_s = time.perf_counter() - t0
+
+    def setup():
+        """A config-3 drafter with the corpus pre-filled (harvests of 16
+        documents; each rebuild waited for, so no document is dropped)."""
+        d = SuffixGPUDrafter(k=16, device=dev, max_pattern_len=32,
+                             max_occurrences=128, num_backoff=8,
+                             enable_global=True, global_capacity=1 << 22,
+                             delta_capacity=1 << 16, rebuild_threshold=32768,
+                             rebuild_stream=torch.cuda.Stream(dev))
+        gi = d.global_index
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        per = 16
+        for i in range(0, docs.shape[0], per):
+            d.harvest_rows([docs[j] for j in
+                            range(i, min(i + per, docs.shape[0]))],
+                           [docs.shape[1]] * min(per, docs.shape[0] - i))
+            gi.wait_rebuild()
+        gi.wait_rebuild()
+        torch.cuda.synchronize()
+        return d, gi, time.perf_counter() - t0
+
+    d, gi, prefill_s = setup()
     prefill_rebuilds = gi.rebuilds
     prefill_builds = len(gi.build_log)
     tok = torch.from_numpy(data["token_ids"]).to(dev)
@@ -880,6 +949,7 @@ def run_global(args, dev) -> dict:
     torch.cuda.synchronize()
     full_same_ms = (time.perf_counter() - tf) * 1e3
     del scratch
+    graph_loop = _global_graph_loop(args, setup, data, samp, q_host, dev)
     # the propose step alone, replayed from a CUDA graph (no harvest)
     n_g = torch.from_numpy(data["num_tokens"]).to(dev)
     tok_g = tok.clone()
@@ -920,6 +990,7 @@ def run_global(args, dev) -> dict:
                         "suffix array (sg_suffix_array_append), full = "
                         "from-scratch build; host wall time of each build "
                         "on its stream (background thread in the loop)"},
+            "graph_loop": graph_loop,
             "graph_propose_us": graph_us,
             "graph_propose_rows_per_s": b / (graph_us * 1e-6),
             "workload": "config3: 4096 x 1024 template corpus (64 templates "

@@ -53,10 +53,16 @@ class _Side:
 
 
 def _run_loop(side: _Side, data: dict, steps: int, harvest_per_step: int,
-              prefill=None, check_every=None):
+              prefill=None, check_every=None, graph: bool = False):
     """Optional bulk prefill of the global index, then per step: harvest
     ``harvest_per_step`` rows of the batch at their current counts, poll,
-    propose_with_update. Returns the per-step outputs and the final state."""
+    propose_with_update. Returns the per-step outputs and the final state.
+
+    ``graph`` (GPU side): step 0 runs eagerly on a capture stream (it
+    creates the side streams and buffers), then propose_with_update is
+    captured once into a CUDA graph over static count and sampled-id
+    buffers (the graph writes the new counts back into its count buffer)
+    and every later step replays it."""
     d = side.d
     if prefill is not None:
         d.global_index.load_documents([side.arr(x) for x in prefill])
@@ -65,6 +71,7 @@ def _run_loop(side: _Side, data: dict, steps: int, harvest_per_step: int,
     b = data["token_ids"].shape[0]
     out = {"draft": [], "num_valid": [], "new_counts": [], "active_len": [],
            "delta_len": []}
+    cap = cg = None
     for j in range(steps):
         if harvest_per_step:
             rows = [(harvest_per_step * j + i) % b
@@ -72,8 +79,26 @@ def _run_loop(side: _Side, data: dict, steps: int, harvest_per_step: int,
             cnt = side.host(n)
             d.harvest_finished(rows, [int(cnt[r]) for r in rows], tok)
             d.poll()
-        draft, nv, n = d.propose_with_update(n, tok,
-                                             side.arr(data["sampled"][j]))
+        if graph and j == 0:
+            cap = torch.cuda.Stream()
+            cap.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(cap):
+                draft, nv, n = d.propose_with_update(
+                    n, tok, side.arr(data["sampled"][j]))
+            torch.cuda.synchronize()
+            n = n.clone()  # the static count buffer
+            samp_s = side.arr(data["sampled"][min(1, steps - 1)])
+            cg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(cg, stream=cap):
+                g_draft, g_nv, g_n = d.propose_with_update(n, tok, samp_s)
+                n.copy_(g_n)
+        elif graph:
+            samp_s.copy_(side.arr(data["sampled"][j]))
+            cg.replay()
+            draft, nv = g_draft, g_nv
+        else:
+            draft, nv, n = d.propose_with_update(n, tok,
+                                                 side.arr(data["sampled"][j]))
         out["draft"].append(side.host(draft))
         out["num_valid"].append(side.host(nv))
         out["new_counts"].append(side.host(n))
@@ -84,6 +109,7 @@ def _run_loop(side: _Side, data: dict, steps: int, harvest_per_step: int,
     res = {k: np.stack(v) if v and isinstance(v[0], np.ndarray)
            else np.array(v) for k, v in out.items()}
     res["final_tokens"] = side.host(tok)
+    del cg
     gi = d.global_index
     if gi is not None:
         res["corpus"] = side.host(gi.corpus)
@@ -178,6 +204,28 @@ def test_config3_full_size_loop_vs_oracle():
     assert g["rebuilds"] >= 3          # the prefill's two, then the loop's
     assert (o["active_len"] > (1 << 22) - 4096).all()
     assert (o["num_valid"] > 0).mean() > 0.5
+
+
+def test_config3_loop_with_captured_propose_vs_oracle():
+    """The config-3 loop (template corpus, harvested rows, a poll every
+    step, synchronous rebuilds that evict and swap in place) with
+    propose_with_update captured once into a CUDA graph and replayed on
+    every step after the first: drafts, counts, rows and the index equal
+    the oracle's eager loop, across every rebuild."""
+    from suffixgpu_b200 import SuffixGPUDrafter
+    data = wl.config3(seed=34, n_docs=512, doc_len=256, b=16, s=1024,
+                      steps=8)
+    cfg = dict(k=16, max_pattern_len=32, max_occurrences=128, num_backoff=8,
+               enable_global=True, global_capacity=1 << 17,
+               delta_capacity=1 << 13, rebuild_threshold=2048)
+    prefill = list(data["corpus_docs"])
+    g = _run_loop(_Side(SuffixGPUDrafter(device=DEV, **cfg), True), data,
+                  8, 4, prefill, graph=True)
+    o = _run_loop(_Side(so.SuffixDrafter(**cfg), False), data, 8, 4,
+                  prefill)
+    _assert_same(g, o, _LOOP_KEYS + _INDEX_KEYS)
+    assert g["rebuilds"] >= 4
+    assert (o["num_valid"] > 0).mean() > 0.3
 
 
 def test_config2_all_decode_steps_vs_oracle():
