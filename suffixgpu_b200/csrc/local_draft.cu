@@ -15,15 +15,14 @@
 //      (update_state semantics).
 //   2. match_back for every end position i < q. Each warp owns a contiguous
 //      segment of positions and appends the nonzero ones, in position order,
-//      to its own hit list (one packed prefix sum per 256 words, no
+//      to its own hit list (one prefix sum per 1024-token chunk, no
 //      block-wide scan), then turns its histogram of the values into
 //      #{mb >= L} per length. The reference's topk over [B,S] becomes a
 //      count over these: the t-th largest value is the largest L with
 //      #{mb >= L} >= t.
-//   3. The earliest R occurrences of each candidate: with few hits the
-//      candidate's warp walks the lists in order (32 entries per ballot);
-//      otherwise every warp writes its qualifying hits at the offset the
-//      per-warp counts give. One warp per candidate then expands its
+//   3. The earliest R occurrences of each candidate: every warp writes its
+//      qualifying hits at the offset the per-warp counts give. One warp per
+//      candidate then expands its
 //      continuation chain (sg_vote.cuh) reading continuations straight from
 //      the shared row, stopping at the candidate's spec cap.
 //   4. argmax(score + f32(cand) * 1e-6) and the masked draft write.
@@ -43,7 +42,6 @@ namespace sg {
 constexpr int kLocalThreads = 256;
 constexpr int kLocalWarps = kLocalThreads / 32;
 constexpr int kMaxCand = 16;  // candidates with threshold 2^c <= S (S < 2^16)
-constexpr int kWalkHits = 256;  // rows with at most this many hits: walk
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 
@@ -541,14 +539,11 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
   const int cand_lane =
       warp_candidates(whist, P, C, p.min_match_len, warp == 0 ? cge : nullptr);
   if (warp == 0 && lane < C) cand_s[lane] = cand_lane;
-  int total_hits = 0;
-#pragma unroll
-  for (int w = 0; w < kLocalWarps; ++w) total_hits += wlen[w];
-  // Few hits: each candidate's warp walks every list itself (no extra
-  // barrier). Many hits: every warp writes its qualifying hits at the
-  // offset given by the per-warp counts of the warps before it.
-  const bool walk = total_hits <= kWalkHits;
-  if (!walk) {
+  // Every warp writes its qualifying hits for each candidate at the offset
+  // given by the per-warp counts of the warps before it (a candidate's warp
+  // walking all the lists itself measured 4-4.5 k cycles on light rows,
+  // more than this pass and its barrier).
+  {
     // earliest R end positions per candidate (local_matcher.py:160-184)
     for (int c = 0; c < C; ++c) {
       const int cand = __shfl_sync(SG_FULL_MASK, cand_lane, c);
@@ -565,21 +560,32 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
         const int lim = nh < room ? nh : room;
         for (int i = lane; i < lim; i += 32) oc[i] = my_hits[i] >> 8;
       } else {
+        // four chunks of 32 hits per round: their loads and ballots go
+        // out together (a slot past nh is in the buffer and unused)
         int got = 0;
-        for (int i0 = 0; i0 < nh && got < k && got < room; i0 += 32) {
-          const int i = i0 + lane;
-          const int ex = my_hits[i];  // past nh: in the buffer, unused
-          const int e = i < nh ? ex : 0;
-          const bool hit = i < nh && (e & 0xff) >= cand;
-          const unsigned bal = __ballot_sync(SG_FULL_MASK, hit);
-          const int r = got + __popc(bal & lt_mask);
-          if (hit && r < room) oc[r] = e >> 8;
-          got += __popc(bal);
+        for (int i0 = 0; i0 < nh && got < k && got < room; i0 += 128) {
+          int ev[4];
+          unsigned bv[4];
+#pragma unroll
+          for (int qd = 0; qd < 4; ++qd) {
+            const int i = i0 + 32 * qd + lane;
+            const int ex = my_hits[i];
+            ev[qd] = i < nh ? ex : 0;
+          }
+#pragma unroll
+          for (int qd = 0; qd < 4; ++qd)
+            bv[qd] = __ballot_sync(SG_FULL_MASK, (ev[qd] & 0xff) >= cand);
+#pragma unroll
+          for (int qd = 0; qd < 4; ++qd) {
+            const int r = got + __popc(bv[qd] & lt_mask);
+            if (((bv[qd] >> lane) & 1u) && r < room) oc[r] = ev[qd] >> 8;
+            got += __popc(bv[qd]);
+          }
         }
       }
     }
-    __syncthreads();
   }
+  __syncthreads();
 
   // ---- 3b. one warp per candidate: vote + score --------------------------
   for (int c = warp; c < C; c += kLocalWarps) {
@@ -595,29 +601,7 @@ __global__ void __launch_bounds__(kLocalThreads, RJ > 8 ? 1 : 2)
     }
     const int* oc = occ_s + c * R;
     int n = 0;
-    if (walk) {
-      // earliest R end positions with mb >= cand, in position order
-      int* ocw = occ_s + c * R;
-      for (int w = 0; w < kLocalWarps && n < R; ++w) {
-        const int kw = whist[w * hstride + cand];  // qualifying entries
-        if (kw == 0) continue;
-        const int* lst = hits + static_cast<size_t>(w) * seg * 4;
-        const int len = wlen[w];
-        const int stop = n + kw;
-        for (int i0 = 0; i0 < len && n < stop && n < R; i0 += 32) {
-          const int ex = lst[i0 + lane];  // past len: in the buffer, unused
-          const int e = i0 + lane < len ? ex : 0;
-          const bool hit = (e & 0xff) >= cand;
-          const unsigned bal = __ballot_sync(SG_FULL_MASK, hit);
-          const int r = n + __popc(bal & lt_mask);
-          if (hit && r < R) ocw[r] = e >> 8;
-          n += __popc(bal);
-        }
-      }
-      __syncwarp();
-    } else {
-      for (int w = 0; w < kLocalWarps; ++w) n += whist[w * hstride + cand];
-    }
+    for (int w = 0; w < kLocalWarps; ++w) n += whist[w * hstride + cand];
     if (n > R) n = R;
     // continuation tokens (local_matcher.py:186-195): tok[e + d] if e+d < q
     auto key_of = [&](int i) -> int { return oc[i]; };
