@@ -242,13 +242,13 @@ int sg_build_suffix_array(const int32_t* tokens, int64_t n, int32_t* sa_out,
  * largest n with sg_suffix_array_workspace_size(n) <= 8 MiB (about 155
  * thousand tokens); larger n returns SG_ERR_UNSUPPORTED without launching
  * anything. The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress). All calls share the array: calls whose work
- * overlaps on the GPU (other streams, other host threads) race and must be
- * serialised by the caller. Synchronises `stream` like
- * sg_build_suffix_array. Device memory is never allocated; the first
- * suffix-array build of the process (through either entry point) may make
- * one 4 KiB page-locked host allocation (cudaHostAlloc) for the per-round
- * counts, and falls back to a stack slot when that fails. */
+ * (cudaGetSymbolAddress); make that first call before any stream capture
+ * begins. All calls share the array, which keeps the last call's contents:
+ * calls whose work overlaps on the GPU (other streams, other host threads)
+ * race and must be serialised by the caller. Synchronises `stream` like
+ * sg_build_suffix_array. Nothing is allocated, on the device or the host:
+ * the per-round count read-backs land in a small array on the calling
+ * thread's stack. */
 int sg_build_suffix_array_noalloc(const int32_t* tokens, int64_t n,
                                   int32_t* sa_out, int32_t* rounds_out,
                                   sg_stream_t stream);

@@ -986,7 +986,10 @@ static uint64_t g_count_used = 0;  // bit i: slot i taken
 
 class CountSlot {
  public:
-  CountSlot() {
+  // use_pool false: the reads land in the slot's own stack array (the
+  // allocation-free build may not make the pool's one host allocation)
+  explicit CountSlot(bool use_pool = true) {
+    if (!use_pool) return;
     std::lock_guard<std::mutex> lk(g_count_mu);
     if (!g_count_pool && !g_count_pool_failed) {
       void* p = nullptr;
@@ -1154,10 +1157,14 @@ extern "C" size_t sg_suffix_array_workspace_size(int64_t n) {
   return carve(nullptr, n).bytes;
 }
 
-extern "C" int sg_build_suffix_array(const int32_t* tokens, int64_t n,
-                                     int32_t* sa_out, void* workspace,
-                                     size_t ws_bytes, int32_t* rounds_out,
-                                     sg_stream_t stream) {
+namespace sg {
+
+// The build behind both entry points; host_pool false keeps the per-round
+// count read-backs out of the page-locked slot pool (no host allocation).
+static int build_suffix_array(const int32_t* tokens, int64_t n,
+                              int32_t* sa_out, void* workspace,
+                              size_t ws_bytes, int32_t* rounds_out,
+                              sg_stream_t stream, bool host_pool) {
   sg::NvtxScope nvtx_range("sg_build_suffix_array");
   if (n < 0) return SG_ERR_INVALID;
   if (n >= (int64_t(1) << 31) - 1) return SG_ERR_UNSUPPORTED;
@@ -1176,7 +1183,7 @@ extern "C" int sg_build_suffix_array(const int32_t* tokens, int64_t n,
   if (!workspace || ws_bytes < carve(nullptr, n).bytes)
     return SG_ERR_WORKSPACE;
   SaWorkspace w = carve(workspace, n);
-  CountSlot slot;
+  CountSlot slot(host_pool);
 
   int kcur = 0;
   int err = SG_OK;
@@ -1287,6 +1294,16 @@ extern "C" int sg_build_suffix_array(const int32_t* tokens, int64_t n,
   return check_launch();
 }
 
+}  // namespace sg
+
+extern "C" int sg_build_suffix_array(const int32_t* tokens, int64_t n,
+                                     int32_t* sa_out, void* workspace,
+                                     size_t ws_bytes, int32_t* rounds_out,
+                                     sg_stream_t stream) {
+  return sg::build_suffix_array(tokens, n, sa_out, workspace, ws_bytes,
+                                rounds_out, stream, /*host_pool=*/true);
+}
+
 // ---------------------------------------------------------------------------
 // Allocation-free variant
 // ---------------------------------------------------------------------------
@@ -1357,7 +1374,9 @@ extern "C" int sg_build_suffix_array_noalloc(const int32_t* tokens,
   if (rc != SG_OK) return rc;
   // The build zeroes the per-pass digit totals itself and writes every
   // other scratch region before reading it, so the previous call's leftover
-  // contents need no clearing.
-  return sg_build_suffix_array(tokens, n, sa_out, scratch,
-                               sg::kSaNoAllocScratchBytes, rounds_out, stream);
+  // contents need no clearing. Its count read-backs land on this thread's
+  // stack, not in the page-locked pool (whose creation allocates).
+  return sg::build_suffix_array(tokens, n, sa_out, scratch,
+                                sg::kSaNoAllocScratchBytes, rounds_out, stream,
+                                /*host_pool=*/false);
 }
