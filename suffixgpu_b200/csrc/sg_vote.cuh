@@ -13,15 +13,17 @@
 // (each lane holds up to RJ occurrences and an alive bit per slot). The
 // cost of a depth is its chain of dependent warp operations, so the
 // expansion works in passes of up to LA depths:
-//   * every survivor reads its next LA tokens at once and measures how long
-//     it agrees with the median survivor (the leader); two packed warp sums
-//     per two depths give the leader's count and the voters at each depth,
-//     and every leading depth where the leader's token holds a strict
-//     majority is decided without counting any other token;
+//   * every survivor reads its next LA tokens at once; one packed warp sum
+//     gives the median survivor's (the leader's) count and the voters at
+//     depth d, and when the leader holds a strict majority there, the
+//     survivors' agreement lengths with the leader and two packed warp
+//     sums per two further depths give the same for the rest of the pass:
+//     every leading depth where the leader's token holds a strict majority
+//     is decided without counting any other token;
 //   * a depth without one gets a full vote: <= 32 survivors (one per lane)
 //     count their tokens among the 32 in a shared buffer; more survivors
-//     count the first and the last pending voter's tokens with ballots
-//     (twice at most, stopping once the uncounted votes cannot reach the
+//     count the first and the last pending voter's tokens with ballots (one
+//     round, which ends the vote when the uncounted votes cannot reach the
 //     best count), and only the remainder goes through a per-warp
 //     open-addressing table in shared memory (one CAS insert + one atomic
 //     add per token).
@@ -355,13 +357,15 @@ __device__ __forceinline__ void compact_survivors(int (&e)[RJ], unsigned& amask,
 //                 a valid expansion).
 //
 // A pass reads the next LA depths of every survivor at once and compares
-// them with the median survivor's (the leader's). A survivor's agreement
-// length lcp says at which depths it still votes for the leader's token, so
-// two packed warp sums give, for every depth k of the pass, the leader's
-// count c_k and the voters a_k (survivors that agreed up to k and have a
-// token there). Every leading depth with a strict majority (2 c_k > a_k) is
-// the vote's result without counting any other token; the first depth
-// without one gets a full vote (vote_small, or vote_rest knowing c_k).
+// them with the median survivor's (the leader's). One packed warp sum gives
+// the leader's count c_0 and the voters a_0 at depth d; only when 2 c_0 >
+// a_0 does the pass go on: a survivor's agreement length lcp says at which
+// depths it still votes for the leader's token, so two packed warp sums per
+// two depths give c_k and a_k (survivors that agreed up to k and have a
+// token there) for the rest of the pass. Every leading depth with a strict
+// majority (2 c_k > a_k) is the vote's result without counting any other
+// token; the first depth without one gets a full vote (vote_small, or
+// vote_rest knowing c_k).
 template <int RJ, class KeyFn, class ContFn, class StopFn = NeverStop>
 __device__ ExpandResult warp_expand(KeyFn key_of, ContFn cont, int n_occ,
                                     int K, long long cap, bool stop_at_cap,
